@@ -1,0 +1,195 @@
+/*
+ * b2sq.h — C ABI of the B200 (sm_100a) smoothquant -> int8 GEMM hot path.
+ *
+ * This is the drop-in boundary for the quantized-inference path of
+ * optimized_rocwmma_samples.  In the reference every operator is a HIP
+ * __global__ kernel launched by the host driver of the same sample file; the
+ * entry points below replace those launches one for one, keep the argument
+ * order and meaning (M/N/K, layouts, leading dimensions, scale tensors,
+ * quant_max, output dtype) and add only:
+ *   - an explicit stream (the reference launches on the default stream),
+ *   - a status return in place of CHECK_HIP -> exit(1)
+ *     (reference common.hpp:33-46, rocwmma_smoothquant.cpp:35-37),
+ *   - UNSUPPORTED in place of "print and return" for shapes the kernels do
+ *     not take (reference rocwmma_gemm_quantized.cpp:199-203).
+ *
+ * Ownership: the caller owns every device buffer (the reference drivers
+ * hipMalloc all of them).  No entry point allocates device memory.
+ * Calls are stream-ordered, never synchronise the device and are reentrant.
+ *
+ * Element types: x is IEEE fp16 (the reference's __half); outputs of the GEMM
+ * are fp16, bf16 or raw int32 accumulators.
+ */
+#ifndef B2SQ_H
+#define B2SQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2SQ_API __attribute__((visibility("default")))
+#else
+#define B2SQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; declared here so the header needs
+ * no CUDA include.  NULL means the legacy default stream. */
+struct CUstream_st;
+typedef struct CUstream_st* b2sq_stream_t;
+
+typedef enum {
+    B2SQ_OK = 0,
+    B2SQ_ERR_INVALID_ARG = 1,  /* null pointer, zero-size or inconsistent ld */
+    B2SQ_ERR_UNSUPPORTED = 2,  /* valid request the kernels do not take (alignment) */
+    B2SQ_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed */
+    B2SQ_ERR_TIMEOUT = 4       /* a bounded device-side wait ran out */
+} b2sq_status;
+
+typedef enum { B2SQ_ROW_MAJOR = 0, B2SQ_COL_MAJOR = 1 } b2sq_layout;
+
+typedef enum {
+    B2SQ_F16 = 0,
+    B2SQ_BF16 = 1,
+    B2SQ_I32 = 2  /* raw int32 accumulators, no dequantisation (debug / parity) */
+} b2sq_dtype;
+
+/* ------------------------------------------------------------------------ */
+/* SmoothQuant                                                              */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Replaces kernel_smoothquant (reference rocwmma_smoothquant.cpp:58-63,
+ * launch :153-155).  For every row m of x[M,N] (row-major, ld = N):
+ *   xs[n]        = float(x[m,n]) * smooth_scale[n]
+ *   row_scale[m] = max_n |xs[n]| / quant_max
+ *   inv          = row_scale[m] > 0 ? 1 / row_scale[m] : 0
+ *   y[m,n]       = int8(clamp(rint(xs[n] * inv), -quant_max, quant_max))
+ * with the reference's fp32 operation order (:83-84, :95, :98, :110-113).
+ * Any N is accepted (the reference's scalar tail, :87-89 / :118-121).
+ * M == 0 is a no-op.
+ */
+B2SQ_API b2sq_status b2sq_smoothquant(const void* x_f16, const float* smooth_scale,
+                             int8_t* y, float* row_scale,
+                             uint32_t M, uint32_t N, float quant_max,
+                             b2sq_stream_t stream);
+
+/*
+ * Replaces kernel_moe_smoothquant (reference rocwmma_moe_smoothquant.cpp:69-76,
+ * launch :179-182).  For token t and slot k < topk with e = topk_ids[t*topk+k]:
+ *   output row r = row_perm ? row_perm[t*topk+k] : t*topk+k
+ *   qy[r,:], row_scale[r] = smoothquant(x[t,:], smooth_scale[e,:])
+ * An expert id outside [0, experts) leaves row r unwritten (reference :86-87);
+ * so does a negative row_perm entry.  row_perm lets a caller write rows
+ * straight into expert-sorted order; NULL gives the reference's order.
+ */
+B2SQ_API b2sq_status b2sq_moe_smoothquant(const void* x_f16, const float* smooth_scale,
+                                 const int32_t* topk_ids, int8_t* qy,
+                                 float* row_scale, uint32_t tokens,
+                                 uint32_t hidden, uint32_t topk,
+                                 uint32_t experts, float quant_max,
+                                 const int32_t* row_perm,
+                                 b2sq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* int8 x int8 -> int32 GEMM with fused dequant epilogue                    */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Replaces gemm_quant_tensor_scale (reference rocwmma_gemm_quantized.cpp:127-132)
+ * and implements its documented, unimplemented "Mode 2 (row-col-scale)"
+ * (:20, :26):
+ *   acc[m,n] = sum_k int32(a[m,k]) * int32(b[k,n])            (exact int32)
+ *   c[m,n]   = cvt_rn(float(acc[m,n]) * (sa * sb))             (c_type F16/BF16)
+ *   c[m,n]   = acc[m,n]                                        (c_type I32)
+ * where sa = scale_a_row ? scale_a_row[m] : scale_a and
+ *       sb = scale_b_col ? scale_b_col[n] : scale_b
+ * (the scale product first, mirroring :189-193).
+ *
+ * Layouts: a is [M,K], row-major (lda >= K) or column-major (lda >= M, the
+ * reference's layout :92); b is [K,N], column-major (ldb >= K, i.e. K-major
+ * weights) or row-major (ldb >= N, the reference's layout :93); c is row-major
+ * [M,N] with ldc >= N (reference :94).
+ * Requirements (else UNSUPPORTED): a, b 16-byte aligned, lda and ldb
+ * multiples of 16.  M, N, K need not be tile multiples.
+ *
+ * workspace: optional int32 scratch for stream-K splitting of tiles across
+ * SMs.  Query its size with b2sq_gemm_i8_workspace_size.  It must be zero
+ * filled before its first use; every completed call leaves it zero filled
+ * again.  NULL (or too small) disables stream-K; results are identical either
+ * way (int32 sums are exact and order independent).
+ */
+B2SQ_API b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k,
+                         const int8_t* a, b2sq_layout la, uint32_t lda,
+                         const int8_t* b, b2sq_layout lb, uint32_t ldb,
+                         void* c, b2sq_dtype c_type, uint32_t ldc,
+                         const float* scale_a_row, const float* scale_b_col,
+                         float scale_a, float scale_b,
+                         void* workspace, size_t workspace_bytes,
+                         b2sq_stream_t stream);
+
+/* Bytes of workspace that let b2sq_gemm_i8 use stream-K for this shape
+ * (0 when the chosen schedule never splits a tile).  Host only. */
+B2SQ_API b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k,
+                                        b2sq_layout la, b2sq_layout lb,
+                                        size_t* bytes);
+
+/*
+ * The schedule b2sq_gemm_i8 would run for a shape (host only, no CUDA call):
+ * tile, operand swap, number of persistent CTAs and the stream-K split.
+ * Exposed so the scheduler's coverage can be checked without a GPU.
+ */
+typedef struct {
+    uint32_t swap_ab;        /* 1: computes C^T = B^T A^T (skinny M) */
+    uint32_t tile_m;         /* MMA M of one tile (rows of the A operand) */
+    uint32_t tile_n;         /* MMA N of one tile */
+    uint32_t tile_k;         /* K elements per pipeline stage */
+    uint32_t stages;
+    uint32_t tiles_m, tiles_n, k_blocks;
+    uint32_t ctas;           /* persistent CTAs launched */
+    uint32_t dp_tiles;       /* tiles computed whole, in data-parallel order */
+    uint32_t sk_iters_per_cta_floor; /* stream-K k-blocks per CTA (floor) */
+    uint64_t sk_iters;       /* total stream-K k-blocks over the tail tiles */
+} b2sq_gemm_plan;
+
+B2SQ_API b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k,
+                              b2sq_layout la, b2sq_layout lb,
+                              int use_stream_k, uint32_t num_sms,
+                              b2sq_gemm_plan* plan);
+
+/* ------------------------------------------------------------------------ */
+/* Diagnostics                                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Static string for a status code. */
+B2SQ_API const char* b2sq_status_string(b2sq_status s);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+B2SQ_API const char* b2sq_last_error_message(void);
+
+/*
+ * Reads and clears the device status word that bounded device-side waits set
+ * when they give up (synchronises `stream`).  B2SQ_OK if no wait ran out,
+ * B2SQ_ERR_TIMEOUT otherwise; *where (nullable) receives the site code.
+ */
+B2SQ_API b2sq_status b2sq_last_device_error(b2sq_stream_t stream, uint32_t* where);
+
+/*
+ * Test hook for the timeout path: launches one CTA that waits on an mbarrier
+ * nothing ever arrives on, with a wait limit of timeout_us microseconds, and
+ * returns what b2sq_last_device_error reports afterwards (B2SQ_ERR_TIMEOUT
+ * when the limit worked).  Touches no caller memory.
+ */
+B2SQ_API b2sq_status b2sq_debug_bounded_wait(uint32_t timeout_us, b2sq_stream_t stream);
+
+/* Library version string. */
+B2SQ_API const char* b2sq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2SQ_H */

@@ -1,0 +1,223 @@
+"""Host-side mirror of the reference operators over the C ABI.
+
+PyTorch supplies device memory and the current stream; every computation is
+one call into libb2sq.so.  Names and argument meaning follow the reference:
+
+=========================  ===================================================
+this module                reference operator (file:line)
+=========================  ===================================================
+``smoothquant``            kernel_smoothquant, rocwmma_smoothquant.cpp:58-63
+``moe_smoothquant``        kernel_moe_smoothquant, rocwmma_moe_smoothquant.cpp:69-76
+``gemm_quant``             gemm_quant_tensor_scale, rocwmma_gemm_quantized.cpp:127-132
+                           (+ the per-row x per-column mode of its header, :20/:26)
+=========================  ===================================================
+
+Errors: the reference exits on a HIP error (CHECK_HIP, common.hpp:33-46) and
+prints-and-returns on unsupported GEMM shapes (rocwmma_gemm_quantized.cpp:199-203);
+here both raise :class:`B2sqError` carrying the library's status code.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import B2sqError, GemmPlan  # noqa: F401  (re-export)
+
+ROW_MAJOR = _lib.ROW_MAJOR
+COL_MAJOR = _lib.COL_MAJOR
+
+_DTYPE_CODE = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.int32: _lib.I32}
+
+
+def _stream_ptr(stream: Optional[torch.cuda.Stream], device: torch.device) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return s.cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("libb2sq operators take CUDA tensors (device memory)")
+        dev = t.device if dev is None else dev
+        if t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def smoothquant(x: torch.Tensor, smooth_scale: torch.Tensor, quant_max: float = 127.0,
+                y: Optional[torch.Tensor] = None, row_scale: Optional[torch.Tensor] = None,
+                stream: Optional[torch.cuda.Stream] = None):
+    """x fp16 [M, N] row-major, smooth_scale fp32 [N] -> (y int8 [M, N], row_scale fp32 [M])."""
+    if x.dtype != torch.float16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous fp16 [M, N] tensor")
+    M, N = x.shape
+    if smooth_scale.dtype != torch.float32 or smooth_scale.numel() != N or not smooth_scale.is_contiguous():
+        raise ValueError("smooth_scale must be a contiguous fp32 [N] tensor")
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.int8, device=x.device)
+    if row_scale is None:
+        row_scale = torch.empty((M,), dtype=torch.float32, device=x.device)
+    dev = _need_cuda(x, smooth_scale, y, row_scale)
+    lib = _lib.load()
+    st = lib.b2sq_smoothquant(x.data_ptr(), smooth_scale.data_ptr(), y.data_ptr(), row_scale.data_ptr(),
+                              M, N, float(quant_max), _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_smoothquant")
+    return y, row_scale
+
+
+def moe_smoothquant(x: torch.Tensor, smooth_scale: torch.Tensor, topk_ids: torch.Tensor,
+                    quant_max: float = 127.0, qy: Optional[torch.Tensor] = None,
+                    row_scale: Optional[torch.Tensor] = None, row_perm: Optional[torch.Tensor] = None,
+                    out_rows: Optional[int] = None, stream: Optional[torch.cuda.Stream] = None):
+    """x fp16 [T, H], smooth_scale fp32 [E, H], topk_ids int32 [T, topk]
+    -> (qy int8 [rows, H], row_scale fp32 [rows]); rows = T*topk unless given."""
+    if x.dtype != torch.float16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous fp16 [tokens, hidden] tensor")
+    T, H = x.shape
+    if smooth_scale.dtype != torch.float32 or smooth_scale.dim() != 2 or smooth_scale.shape[1] != H:
+        raise ValueError("smooth_scale must be fp32 [experts, hidden]")
+    if topk_ids.dtype != torch.int32 or topk_ids.dim() != 2 or topk_ids.shape[0] != T:
+        raise ValueError("topk_ids must be int32 [tokens, topk]")
+    E, topk = smooth_scale.shape[0], topk_ids.shape[1]
+    rows = out_rows if out_rows is not None else T * topk
+    if qy is None:
+        qy = torch.zeros((rows, H), dtype=torch.int8, device=x.device)
+    if row_scale is None:
+        row_scale = torch.zeros((rows,), dtype=torch.float32, device=x.device)
+    if row_perm is not None and (row_perm.dtype != torch.int32 or row_perm.numel() != T * topk):
+        raise ValueError("row_perm must be int32 with tokens*topk entries")
+    dev = _need_cuda(x, smooth_scale, topk_ids, qy, row_scale, row_perm)
+    lib = _lib.load()
+    st = lib.b2sq_moe_smoothquant(x.data_ptr(), smooth_scale.contiguous().data_ptr(),
+                                  topk_ids.contiguous().data_ptr(), qy.data_ptr(), row_scale.data_ptr(),
+                                  T, H, topk, E, float(quant_max), _ptr(row_perm), _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_moe_smoothquant")
+    return qy, row_scale
+
+
+def _layout_of(t: torch.Tensor, rows: int, cols: int):
+    """(layout, ld) of a 2-D view [rows, cols]; row-major if stride(1)==1, col-major if stride(0)==1."""
+    if t.dim() != 2 or tuple(t.shape) != (rows, cols):
+        raise ValueError(f"expected a [{rows}, {cols}] tensor, got {tuple(t.shape)}")
+    s0, s1 = t.stride()
+    if s1 == 1 and (rows <= 1 or s0 >= cols):
+        return ROW_MAJOR, (s0 if rows > 1 else max(s0, cols))
+    if s0 == 1 and (cols <= 1 or s1 >= rows):
+        return COL_MAJOR, (s1 if cols > 1 else max(s1, rows))
+    raise ValueError("operand must be row-major or column-major (unit stride in one dimension)")
+
+
+def plan(m: int, n: int, k: int, la: int = ROW_MAJOR, lb: int = COL_MAJOR, use_stream_k: bool = True,
+         num_sms: int = 0) -> GemmPlan:
+    """The schedule b2sq_gemm_i8 runs for this shape (host only when num_sms > 0)."""
+    lib = _lib.load()
+    p = GemmPlan()
+    _lib.check(lib.b2sq_gemm_i8_plan(m, n, k, la, lb, int(use_stream_k), num_sms, C.byref(p)),
+               "b2sq_gemm_i8_plan")
+    return p
+
+
+class Workspace:
+    """Zero-filled, reusable stream-K workspace (one per device), grown on demand.
+
+    The library leaves it zero-filled after every completed call, so it is
+    cleared only when (re)allocated.  Calls sharing it must be stream-ordered.
+    """
+
+    def __init__(self):
+        self._bufs: dict[int, torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> Optional[torch.Tensor]:
+        if nbytes == 0:
+            return None
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        buf = self._bufs.get(idx)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(((nbytes + 255) // 256) * 256, dtype=torch.uint8, device=device)
+            self._bufs[idx] = buf
+        return buf
+
+
+_default_ws = Workspace()
+
+
+def workspace_size(m: int, n: int, k: int, la: int = ROW_MAJOR, lb: int = COL_MAJOR) -> int:
+    lib = _lib.load()
+    out = C.c_size_t(0)
+    _lib.check(lib.b2sq_gemm_i8_workspace_size(m, n, k, la, lb, C.byref(out)), "b2sq_gemm_i8_workspace_size")
+    return out.value
+
+
+def gemm_quant(a: torch.Tensor, b: torch.Tensor, scale_a_row: Optional[torch.Tensor] = None,
+               scale_b_col: Optional[torch.Tensor] = None, scale_a: float = 1.0, scale_b: float = 1.0,
+               out_dtype: torch.dtype = torch.bfloat16, c: Optional[torch.Tensor] = None,
+               stream_k: bool = True, workspace: Optional[Workspace] = None,
+               stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """c[M,N] = cvt(float(a[M,K] @ b[K,N]) * (sa[m] * sb[n])), int8 operands, int32 accumulation.
+
+    a: int8 [M, K] row- or column-major; b: int8 [K, N] column-major (K-major
+    weights, ``w.t()`` of a contiguous [N, K]) or row-major.  out_dtype
+    float16 / bfloat16 / int32 (raw accumulators).
+    """
+    if a.dtype != torch.int8 or b.dtype != torch.int8:
+        raise ValueError("a and b must be int8")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError(f"shape mismatch: a {tuple(a.shape)} b {tuple(b.shape)}")
+    M, K = a.shape
+    N = b.shape[1]
+    la, lda = _layout_of(a, M, K)
+    lb, ldb = _layout_of(b, K, N)
+    if out_dtype not in _DTYPE_CODE:
+        raise ValueError("out_dtype must be float16, bfloat16 or int32")
+    if c is None:
+        c = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    if c.dtype != out_dtype or c.dim() != 2 or tuple(c.shape) != (M, N) or c.stride(1) != 1:
+        raise ValueError("c must be a row-major [M, N] tensor of out_dtype")
+    for s, nm, L in ((scale_a_row, "scale_a_row", M), (scale_b_col, "scale_b_col", N)):
+        if s is not None and (s.dtype != torch.float32 or s.numel() != L or not s.is_contiguous()):
+            raise ValueError(f"{nm} must be a contiguous fp32 vector of {L}")
+    dev = _need_cuda(a, b, c, scale_a_row, scale_b_col)
+    ws, ws_bytes = None, 0
+    if stream_k:
+        need = workspace_size(M, N, K, la, lb)
+        ws = (workspace or _default_ws).get(dev, need)
+        ws_bytes = 0 if ws is None else ws.numel()
+    lib = _lib.load()
+    st = lib.b2sq_gemm_i8(M, N, K, a.data_ptr(), la, lda, b.data_ptr(), lb, ldb, c.data_ptr(),
+                          _DTYPE_CODE[out_dtype], c.stride(0) if M > 1 else N, _ptr(scale_a_row),
+                          _ptr(scale_b_col), float(scale_a), float(scale_b), _ptr(ws), ws_bytes,
+                          _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_gemm_i8")
+    return c
+
+
+def last_device_error(stream: Optional[torch.cuda.Stream] = None) -> int:
+    """Reads/clears the device status word; returns the wait-site code (0 = none)."""
+    lib = _lib.load()
+    where = C.c_uint32(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib.b2sq_last_device_error(_stream_ptr(stream, dev), C.byref(where))
+    return where.value
+
+
+def debug_bounded_wait(timeout_us: int, stream: Optional[torch.cuda.Stream] = None) -> int:
+    """Runs the bounded-wait self test; returns the library status (TIMEOUT expected)."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    return lib.b2sq_debug_bounded_wait(timeout_us, _stream_ptr(stream, dev))
+
+
+# Reference operator names.
+kernel_smoothquant = smoothquant
+kernel_moe_smoothquant = moe_smoothquant
+gemm_quant_tensor_scale = gemm_quant

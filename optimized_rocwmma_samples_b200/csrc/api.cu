@@ -1,0 +1,310 @@
+// api.cu — the extern "C" boundary declared in include/b2sq.h.
+//
+// Every entry point validates its arguments on the host before any CUDA call
+// (so argument errors are reported without a device), maps the request onto
+// the kernels and returns a status.  Nothing here allocates device memory,
+// synchronises the device or exits the process (the reference's CHECK_HIP
+// exits, common.hpp:33-46; its GEMM driver prints and returns on shapes it
+// does not take, rocwmma_gemm_quantized.cpp:199-203).
+#include "../../include/b2sq.h"
+#include "kernels.h"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace {
+
+thread_local char g_msg[256] = "";
+
+b2sq_status fail(b2sq_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+b2sq_status fail(b2sq_status s, const char* fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return s;
+}
+
+b2sq_status ok()
+{
+    g_msg[0] = '\0';
+    return B2SQ_OK;
+}
+
+b2sq_status cuda_fail(cudaError_t e, const char* where)
+{
+    return fail(B2SQ_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+bool qmax_ok(float q) { return std::isfinite(q) && q > 0.f && q <= 127.f; }
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Streaming multiprocessor count of the current device (cached per device).
+cudaError_t current_sm_count(uint32_t* out)
+{
+    static std::mutex mu;
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+        *out = (uint32_t)cache[dev];
+        return cudaSuccess;
+    }
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    *out = (uint32_t)n;
+    return cudaSuccess;
+}
+
+// Skinny M (decode): compute C^T = B^T A^T so the long N dimension fills the
+// 128-row MMA and the few tokens become a 16..128-wide MMA N.
+bool want_swap(uint32_t m, uint32_t n, b2sq_layout la)
+{
+    return m <= 128 && n >= 2 * m && n >= 256 && la == B2SQ_ROW_MAJOR;
+}
+
+struct Mapped {
+    uint32_t swap;
+    uint32_t Mk, Nk, a_mn, b_mn;
+};
+
+Mapped map_operands(uint32_t m, uint32_t n, b2sq_layout la, b2sq_layout lb)
+{
+    Mapped r{};
+    r.swap = want_swap(m, n, la) ? 1u : 0u;
+    if (r.swap) {
+        r.Mk = n;
+        r.Nk = m;
+        r.a_mn = (lb == B2SQ_ROW_MAJOR) ? 1u : 0u;  // B [K,N] row-major: n contiguous
+        r.b_mn = (la == B2SQ_COL_MAJOR) ? 1u : 0u;
+    } else {
+        r.Mk = m;
+        r.Nk = n;
+        r.a_mn = (la == B2SQ_COL_MAJOR) ? 1u : 0u;  // A [M,K] col-major: m contiguous
+        r.b_mn = (lb == B2SQ_ROW_MAJOR) ? 1u : 0u;
+    }
+    return r;
+}
+
+b2sq_status validate_gemm(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
+                          const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
+                          const float* sa, const float* sb)
+{
+    if (la != B2SQ_ROW_MAJOR && la != B2SQ_COL_MAJOR) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: bad layout of a");
+    if (lb != B2SQ_ROW_MAJOR && lb != B2SQ_COL_MAJOR) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: bad layout of b");
+    if (c_type != B2SQ_F16 && c_type != B2SQ_BF16 && c_type != B2SQ_I32)
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: bad output dtype %d", (int)c_type);
+    if (m == 0 || n == 0) return ok();
+    if (!c) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: c is null");
+    if (ldc < n) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: ldc %u < n %u", ldc, n);
+    if (!aligned(c, c_type == B2SQ_I32 ? 4 : 2)) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: c misaligned");
+    if (k == 0) return ok();
+    if (!a || !b) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: a or b is null");
+    const uint32_t min_lda = la == B2SQ_ROW_MAJOR ? k : m;
+    const uint32_t min_ldb = lb == B2SQ_COL_MAJOR ? k : n;
+    if (lda < min_lda) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: lda %u < %u", lda, min_lda);
+    if (ldb < min_ldb) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: ldb %u < %u", ldb, min_ldb);
+    if ((sa && !aligned(sa, 4)) || (sb && !aligned(sb, 4)))
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: scale vector misaligned");
+    if (!aligned(a, 16) || !aligned(b, 16))
+        return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8: a and b must be 16-byte aligned (TMA)");
+    if (lda % 16 || ldb % 16)
+        return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8: lda (%u) and ldb (%u) must be multiples of 16 (TMA)", lda, ldb);
+    return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b2sq_version(void) { return "b2sq 0.1.0 (sm_100a)"; }
+
+const char* b2sq_status_string(b2sq_status s)
+{
+    switch (s) {
+        case B2SQ_OK: return "ok";
+        case B2SQ_ERR_INVALID_ARG: return "invalid argument";
+        case B2SQ_ERR_UNSUPPORTED: return "unsupported";
+        case B2SQ_ERR_CUDA: return "CUDA error";
+        case B2SQ_ERR_TIMEOUT: return "device wait timed out";
+    }
+    return "unknown status";
+}
+
+const char* b2sq_last_error_message(void) { return g_msg; }
+
+b2sq_status b2sq_smoothquant(const void* x_f16, const float* smooth_scale, int8_t* y, float* row_scale, uint32_t M,
+                             uint32_t N, float quant_max, b2sq_stream_t stream)
+{
+    if (!qmax_ok(quant_max)) return fail(B2SQ_ERR_INVALID_ARG, "smoothquant: quant_max must be in (0, 127]");
+    if (M == 0) return ok();
+    if (!row_scale || (N > 0 && (!x_f16 || !smooth_scale || !y)))
+        return fail(B2SQ_ERR_INVALID_ARG, "smoothquant: null pointer");
+    if (!aligned(x_f16, 2) || !aligned(smooth_scale, 4) || !aligned(row_scale, 4))
+        return fail(B2SQ_ERR_INVALID_ARG, "smoothquant: misaligned pointer");
+    cudaError_t e = b2sq::launch_smoothquant(x_f16, smooth_scale, y, row_scale, M, N, quant_max,
+                                             reinterpret_cast<cudaStream_t>(stream), nullptr);
+    if (e != cudaSuccess) return cuda_fail(e, "smoothquant launch");
+    return ok();
+}
+
+b2sq_status b2sq_moe_smoothquant(const void* x_f16, const float* smooth_scale, const int32_t* topk_ids, int8_t* qy,
+                                 float* row_scale, uint32_t tokens, uint32_t hidden, uint32_t topk, uint32_t experts,
+                                 float quant_max, const int32_t* row_perm, b2sq_stream_t stream)
+{
+    if (!qmax_ok(quant_max)) return fail(B2SQ_ERR_INVALID_ARG, "moe_smoothquant: quant_max must be in (0, 127]");
+    if (tokens == 0 || topk == 0) return ok();
+    if (!topk_ids || !row_scale || (hidden > 0 && (!x_f16 || !qy)) || (experts > 0 && hidden > 0 && !smooth_scale))
+        return fail(B2SQ_ERR_INVALID_ARG, "moe_smoothquant: null pointer");
+    if (!aligned(x_f16, 2) || !aligned(smooth_scale, 4) || !aligned(row_scale, 4) || !aligned(topk_ids, 4) ||
+        !aligned(row_perm, 4))
+        return fail(B2SQ_ERR_INVALID_ARG, "moe_smoothquant: misaligned pointer");
+    if ((uint64_t)tokens * topk > 0xffffffffull)
+        return fail(B2SQ_ERR_INVALID_ARG, "moe_smoothquant: tokens*topk overflows 32 bits");
+    cudaError_t e = b2sq::launch_moe_smoothquant(x_f16, smooth_scale, topk_ids, qy, row_scale, tokens, hidden, topk,
+                                                 experts, quant_max, row_perm,
+                                                 reinterpret_cast<cudaStream_t>(stream), nullptr);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_smoothquant launch");
+    return ok();
+}
+
+b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k, b2sq_layout la, b2sq_layout lb, int use_stream_k,
+                              uint32_t num_sms, b2sq_gemm_plan* plan)
+{
+    if (!plan) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_plan: plan is null");
+    if ((la != B2SQ_ROW_MAJOR && la != B2SQ_COL_MAJOR) || (lb != B2SQ_ROW_MAJOR && lb != B2SQ_COL_MAJOR))
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_plan: bad layout");
+    if (num_sms == 0) {
+        cudaError_t e = current_sm_count(&num_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm_i8_plan: SM count");
+    }
+    const Mapped mp = map_operands(m, n, la, lb);
+    b2sq::GemmSchedule s;
+    b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.b_mn, use_stream_k != 0, num_sms, s);
+    std::memset(plan, 0, sizeof(*plan));
+    plan->swap_ab = mp.swap;
+    plan->tile_m = b2sq::kTileM;
+    plan->tile_n = s.tile_n;
+    plan->tile_k = b2sq::kTileK;
+    plan->stages = s.stages;
+    plan->tiles_m = s.tiles_m;
+    plan->tiles_n = s.tiles_n;
+    plan->k_blocks = s.k_blocks;
+    plan->ctas = s.ctas;
+    plan->dp_tiles = s.dp_tiles;
+    plan->sk_iters = s.sk_iters;
+    plan->sk_iters_per_cta_floor = s.ctas ? (uint32_t)(s.sk_iters / s.ctas) : 0;
+    return ok();
+}
+
+b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k, b2sq_layout la, b2sq_layout lb,
+                                        size_t* bytes)
+{
+    if (!bytes) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_workspace_size: bytes is null");
+    if ((la != B2SQ_ROW_MAJOR && la != B2SQ_COL_MAJOR) || (lb != B2SQ_ROW_MAJOR && lb != B2SQ_COL_MAJOR))
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_workspace_size: bad layout");
+    *bytes = 0;
+    if (m == 0 || n == 0 || k == 0) return ok();
+    uint32_t sms = 0;
+    cudaError_t e = current_sm_count(&sms);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_i8_workspace_size: SM count");
+    const Mapped mp = map_operands(m, n, la, lb);
+    b2sq::GemmSchedule s;
+    b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.b_mn, true, sms, s);
+    *bytes = s.workspace_bytes;
+    return ok();
+}
+
+b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
+                         const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
+                         const float* scale_a_row, const float* scale_b_col, float scale_a, float scale_b,
+                         void* workspace, size_t workspace_bytes, b2sq_stream_t stream)
+{
+    b2sq_status st = validate_gemm(m, n, k, a, la, lda, b, lb, ldb, c, c_type, ldc, scale_a_row, scale_b_col);
+    if (st != B2SQ_OK || m == 0 || n == 0) return st;
+    cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+    const size_t esz = c_type == B2SQ_I32 ? 4 : 2;
+    if (k == 0) {  // empty sum: every output is +0
+        cudaError_t e = cudaMemset2DAsync(c, (size_t)ldc * esz, 0, (size_t)n * esz, m, cs);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm_i8: zero fill");
+        return ok();
+    }
+    uint32_t sms = 0;
+    cudaError_t e = current_sm_count(&sms);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_i8: SM count");
+
+    const Mapped mp = map_operands(m, n, la, lb);
+    b2sq::GemmProblem p{};
+    p.Mk = mp.Mk;
+    p.Nk = mp.Nk;
+    p.K = k;
+    p.a_mn_major = mp.a_mn;
+    p.b_mn_major = mp.b_mn;
+    p.c = c;
+    p.ldc = ldc;
+    p.c_type = (int)c_type;
+    p.transpose_out = (int)mp.swap;
+    if (mp.swap) {
+        p.a = b;
+        p.lda = ldb;
+        p.b = a;
+        p.ldb = lda;
+        p.row_scale_vec = scale_b_col;
+        p.col_scale_vec = scale_a_row;
+        p.row_scale = scale_b;
+        p.col_scale = scale_a;
+    } else {
+        p.a = a;
+        p.lda = lda;
+        p.b = b;
+        p.ldb = ldb;
+        p.row_scale_vec = scale_a_row;
+        p.col_scale_vec = scale_b_col;
+        p.row_scale = scale_a;
+        p.col_scale = scale_b;
+    }
+    b2sq::GemmSchedule s;
+    b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.b_mn_major, workspace != nullptr, sms, s);
+    if (s.workspace_bytes > 0 && (workspace == nullptr || workspace_bytes < s.workspace_bytes))
+        b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.b_mn_major, false, sms, s);
+    if (s.workspace_bytes > 0 && !aligned(workspace, 256))
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: workspace must be 256-byte aligned");
+    const char* detail = nullptr;
+    e = b2sq::launch_gemm_i8(p, s, workspace, cs, &detail);
+    if (e != cudaSuccess) {
+        if (detail) return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8: %s", detail);
+        return cuda_fail(e, "gemm_i8 launch");
+    }
+    return ok();
+}
+
+b2sq_status b2sq_last_device_error(b2sq_stream_t stream, uint32_t* where)
+{
+    uint32_t v = 0;
+    cudaError_t e = b2sq::read_and_clear_device_status(reinterpret_cast<cudaStream_t>(stream), &v);
+    if (e != cudaSuccess) return cuda_fail(e, "last_device_error");
+    if (where) *where = v;
+    if (v != 0) return fail(B2SQ_ERR_TIMEOUT, "device wait gave up at site %u", v);
+    return ok();
+}
+
+b2sq_status b2sq_debug_bounded_wait(uint32_t timeout_us, b2sq_stream_t stream)
+{
+    if (timeout_us == 0 || timeout_us > 10u * 1000u * 1000u)
+        return fail(B2SQ_ERR_INVALID_ARG, "debug_bounded_wait: timeout_us must be in (0, 10 s]");
+    cudaError_t e = b2sq::launch_debug_bounded_wait((uint64_t)timeout_us * 1000ull,
+                                                    reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "debug_bounded_wait launch");
+    return b2sq_last_device_error(stream, nullptr);
+}
+
+}  // extern "C"

@@ -1,0 +1,662 @@
+// gemm_i8.cu — int8 x int8 -> int32 GEMM with a fused per-row x per-column
+// dequant epilogue, for sm_100a (tcgen05 kind::i8, TMEM accumulators, TMA).
+//
+// Replaces gemm_quant_tensor_scale (reference rocwmma_gemm_quantized.cpp:127-195).
+// The reference kernel is a 128x128 macro tile, 2-stage LDS ping-pong, one
+// CTA per output tile, with the epilogue fp16(float(acc) * (scale_a*scale_b))
+// (:188-194).  This kernel keeps that arithmetic and generalises the scales
+// to per-row / per-column vectors (the reference header's Mode 2, :20, :26);
+// the machinery is Blackwell's:
+//
+//  * persistent CTAs (one per SM), warp specialised:
+//      warp 0      TMA producer: 128-byte-swizzled A/B tiles into a ring of
+//                  shared-memory stages (mbarrier full/empty pairs);
+//      warp 1      MMA issuer: one thread issues tcgen05.mma.kind::i8
+//                  (M=128, N=tile_n, K=32 per instruction) into an int32
+//                  accumulator in tensor memory; tcgen05.commit frees stages;
+//      warps 2..5  epilogue: tcgen05.ld of the accumulator, fp32 dequant,
+//                  cvt.rn to fp16/bf16, stores.  Two TMEM accumulators
+//                  alternate so the epilogue of tile i overlaps the main loop
+//                  of tile i+1.
+//  * tile schedule: whole tiles in data-parallel rounds over the CTAs, then
+//    the tail tiles' k-blocks split evenly over all CTAs (stream-K, the
+//    scheme of rocwmma_streamk_gemm.cpp:102-143).  Partial sums are added
+//    with int32 atomics into a workspace (exact, so the result does not
+//    depend on the split); the CTA whose contribution completes a tile's K
+//    range does its epilogue and re-zeroes the workspace.  No CTA ever waits
+//    on another CTA, so the fix-up cannot hang.
+//  * no TMA multicast anywhere (every CTA loads its own tiles).
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+#include <mutex>
+
+namespace b2sq {
+
+namespace {
+
+constexpr uint32_t kThreads = 192;  // 6 warps
+constexpr uint32_t kEpiThreads = 128;
+constexpr uint32_t kABytes = kTileM * kTileK;  // 16 KiB per stage
+constexpr uint32_t kSmemBudget = 232448;       // 227 KiB opt-in limit per CTA
+constexpr uint32_t kBarrierBytes = 256;
+
+__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return kABytes + bn * kTileK; }
+__host__ __device__ constexpr uint32_t num_stages(uint32_t bn)
+{
+    return ((kSmemBudget - 1024 - kBarrierBytes) / stage_bytes(bn)) > 8
+               ? 8
+               : ((kSmemBudget - 1024 - kBarrierBytes) / stage_bytes(bn));
+}
+__host__ __device__ constexpr uint32_t tmem_cols(uint32_t bn)
+{
+    return (2 * bn <= 32) ? 32 : (2 * bn <= 64) ? 64 : (2 * bn <= 128) ? 128 : (2 * bn <= 256) ? 256 : 512;
+}
+
+struct KParams {
+    uint32_t Mk, Nk, K;
+    uint32_t tiles_m, tiles_n, k_blocks;
+    uint32_t dp_tiles, ctas;
+    uint64_t sk_iters;
+    uint32_t a_mn_major, b_mn_major;
+    void* c;
+    uint32_t ldc;
+    int c_type;
+    int transpose_out;
+    int vec_store_ok;
+    const float* row_scale_vec;
+    const float* col_scale_vec;
+    float row_scale, col_scale;
+    int32_t* ws;        // [tail tiles][tile_n][128] int32
+    uint32_t* ws_cnt;   // [tail tiles] k-blocks accumulated so far
+    uint32_t raster_group;
+};
+
+struct Unit {
+    uint32_t tile, k0, k1;
+};
+
+// Work list of one CTA: its data-parallel tiles, then its contiguous range of
+// stream-K k-block iterations over the tail tiles.
+struct UnitIter {
+    uint32_t dp_next;
+    uint64_t sk_pos, sk_end;
+
+    __device__ __forceinline__ void init(const KParams& p)
+    {
+        dp_next = blockIdx.x;
+        sk_pos = (uint64_t)blockIdx.x * p.sk_iters / p.ctas;
+        sk_end = (uint64_t)(blockIdx.x + 1) * p.sk_iters / p.ctas;
+    }
+    __device__ __forceinline__ bool next(const KParams& p, Unit& u)
+    {
+        if (dp_next < p.dp_tiles) {
+            u = {dp_next, 0, p.k_blocks};
+            dp_next += p.ctas;
+            return true;
+        }
+        if (sk_pos < sk_end) {
+            const uint64_t t = sk_pos / p.k_blocks;
+            const uint32_t k0 = (uint32_t)(sk_pos - t * p.k_blocks);
+            const uint64_t rem = sk_end - sk_pos;
+            const uint32_t k1 = (uint32_t)((k0 + rem < p.k_blocks) ? k0 + rem : p.k_blocks);
+            u = {p.dp_tiles + (uint32_t)t, k0, k1};
+            sk_pos += k1 - k0;
+            return true;
+        }
+        return false;
+    }
+};
+
+// Tile index -> (tile_m, tile_n), grouped along M so that CTAs running at the
+// same time share A and B panels in L2.
+__device__ __forceinline__ void tile_coords(const KParams& p, uint32_t t, uint32_t& tm, uint32_t& tn)
+{
+    const uint32_t per_group = p.raster_group * p.tiles_n;
+    const uint32_t g = t / per_group;
+    const uint32_t first_m = g * p.raster_group;
+    const uint32_t gsize = (p.tiles_m - first_m) < p.raster_group ? (p.tiles_m - first_m) : p.raster_group;
+    const uint32_t r = t - g * per_group;
+    tm = first_m + r % gsize;
+    tn = r / gsize;
+}
+
+template <uint32_t BN>
+struct Smem {
+    static constexpr uint32_t ST = num_stages(BN);
+    static constexpr uint32_t SB = stage_bytes(BN);
+    static constexpr uint32_t bar_off = ST * SB;
+    // barrier area (8-byte aligned) after the stages
+    static constexpr uint32_t full_off = bar_off;
+    static constexpr uint32_t empty_off = full_off + 8 * ST;
+    static constexpr uint32_t tfull_off = empty_off + 8 * ST;
+    static constexpr uint32_t tempty_off = tfull_off + 16;
+    static constexpr uint32_t taddr_off = tempty_off + 16;
+    static constexpr uint32_t abort_off = taddr_off + 4;
+    static constexpr uint32_t flag_off = abort_off + 4;
+    static constexpr uint32_t total = bar_off + kBarrierBytes + 1024;
+    static_assert(flag_off + 4 <= bar_off + kBarrierBytes, "barrier area overflow");
+    static_assert(total <= kSmemBudget, "shared memory overflow");
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b)
+{
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16(float a, float b)
+{
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <uint32_t W>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, int32_t (&acc)[W])
+{
+    if constexpr (W == 32) tmem_ld_32x32b_x32(taddr, reinterpret_cast<uint32_t(&)[32]>(acc));
+    else tmem_ld_32x32b_x16(taddr, reinterpret_cast<uint32_t(&)[16]>(acc));
+}
+
+// Dequantises and stores W consecutive kernel columns [col0, col0+W) of
+// kernel row `row` (one thread = one row).
+template <uint32_t W>
+__device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&acc)[W])
+{
+    if (row >= p.Mk) return;
+    if (p.c_type == 2) {  // raw int32
+        int32_t* c = static_cast<int32_t*>(p.c);
+        if (!p.transpose_out) {
+            int32_t* dst = c + (size_t)row * p.ldc + col0;
+            if (p.vec_store_ok && col0 + W <= p.Nk) {
+#pragma unroll
+                for (int j = 0; j < (int)W; j += 4)
+                    *reinterpret_cast<int4*>(dst + j) = make_int4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < (int)W; ++j)
+                    if (col0 + j < p.Nk) dst[j] = acc[j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < (int)W; ++j)
+                if (col0 + j < p.Nk) c[(size_t)(col0 + j) * p.ldc + row] = acc[j];
+        }
+        return;
+    }
+    const float rsc = p.row_scale_vec ? __ldg(p.row_scale_vec + row) : p.row_scale;
+    float v[W];
+#pragma unroll
+    for (int j = 0; j < (int)W; ++j) {
+        const uint32_t col = col0 + j;
+        const float csc = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + col) : 0.f) : p.col_scale;
+        v[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(rsc, csc));
+    }
+    uint16_t* c = static_cast<uint16_t*>(p.c);
+    if (!p.transpose_out) {
+        uint16_t* dst = c + (size_t)row * p.ldc + col0;
+        if (p.vec_store_ok && col0 + W <= p.Nk) {
+#pragma unroll
+            for (int j = 0; j < (int)W; j += 8) {
+                uint4 w;
+                if (p.c_type == 1) {
+                    w = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
+                                   pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
+                } else {
+                    w = make_uint4(pack_f16(v[j], v[j + 1]), pack_f16(v[j + 2], v[j + 3]),
+                                   pack_f16(v[j + 4], v[j + 5]), pack_f16(v[j + 6], v[j + 7]));
+                }
+                *reinterpret_cast<uint4*>(dst + j) = w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < (int)W; ++j) {
+                if (col0 + j < p.Nk) {
+                    dst[j] = p.c_type == 1 ? __bfloat16_as_ushort(__float2bfloat16_rn(v[j]))
+                                           : __half_as_ushort(__float2half_rn(v[j]));
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < (int)W; ++j) {
+            if (col0 + j < p.Nk) {
+                c[(size_t)(col0 + j) * p.ldc + row] = p.c_type == 1 ? __bfloat16_as_ushort(__float2bfloat16_rn(v[j]))
+                                                                    : __half_as_ushort(__float2half_rn(v[j]));
+            }
+        }
+    }
+}
+
+template <uint32_t BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p,
+                   uint64_t wait_limit_ns)
+{
+    using L = Smem<BN>;
+    constexpr uint32_t ST = L::ST;
+    constexpr uint32_t TMEM_COLS = tmem_cols(BN);
+    constexpr uint32_t CW = BN < 32 ? BN : 32;  // columns per tcgen05.ld
+    constexpr uint32_t NCH = BN / CW;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t full_bar = sbase + L::full_off;
+    const uint32_t empty_bar = sbase + L::empty_off;
+    const uint32_t tfull_bar = sbase + L::tfull_off;
+    const uint32_t tempty_bar = sbase + L::tempty_off;
+    volatile uint32_t* taddr_slot = reinterpret_cast<volatile uint32_t*>(smem + L::taddr_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::abort_off);
+    volatile int* epi_flag = reinterpret_cast<volatile int*>(smem + L::flag_off);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < ST; ++s) {
+            mbar_init(full_bar + 8 * s, 1);
+            mbar_init(empty_bar + 8 * s, 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar + 8 * b, 1);
+            mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(sbase + L::taddr_off, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *taddr_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            UnitIter it;
+            it.init(p);
+            Unit u;
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_phase[8];
+            bool issued[8];
+            for (uint32_t s = 0; s < 8; ++s) issued[s] = false, issued_phase[s] = 0;
+            bool ok = true;
+            while (ok && it.next(p, u)) {
+                uint32_t tm, tn;
+                tile_coords(p, u.tile, tm, tn);
+                const int32_t a_row = (int32_t)(tm * kTileM);
+                const int32_t b_row = (int32_t)(tn * BN);
+                for (uint32_t kb = u.k0; kb < u.k1; ++kb) {
+                    if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_bar + 8 * stage;
+                    mbar_arrive_expect_tx(fb, L::SB);
+                    const uint32_t sa = sbase + stage * L::SB;
+                    const uint32_t sb = sa + kABytes;
+                    const int32_t kc = (int32_t)(kb * kTileK);
+                    if (p.a_mn_major) tma_load_2d(sa, &tmA, fb, a_row, kc);
+                    else tma_load_2d(sa, &tmA, fb, kc, a_row);
+                    if (p.b_mn_major) {
+#pragma unroll
+                        for (uint32_t j = 0; j < BN / 128; ++j)
+                            tma_load_2d(sb + j * (128 * kTileK), &tmB, fb, b_row + (int32_t)(j * 128), kc);
+                    } else {
+                        tma_load_2d(sb, &tmB, fb, kc, b_row);
+                    }
+                    issued[stage] = true;
+                    issued_phase[stage] = phase;
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+            }
+            // Drain: every TMA copy this thread issued lands before the CTA
+            // exits (immediate on the normal path).
+            for (uint32_t s = 0; s < ST; ++s)
+                if (issued[s]) mbar_wait(full_bar + 8 * s, issued_phase[s], SITE_PRODUCER_DRAIN, nullptr, wait_limit_ns);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_base = idesc_i8(kTileM, BN, 0, 0);
+            const uint32_t idesc = idesc_base | (p.a_mn_major << 15) | (p.b_mn_major << 16);
+            // Per-instruction (K = 32) descriptor advance inside a stage.
+            const uint32_t a_step = p.a_mn_major ? 32 * 128 : 32;
+            const uint32_t b_step = p.b_mn_major ? 32 * 128 : 32;
+            const uint32_t a_lbo = p.a_mn_major ? 128 * kTileK : 16;
+            const uint32_t b_lbo = p.b_mn_major ? 128 * kTileK : 16;
+            UnitIter it;
+            it.init(p);
+            Unit u;
+            uint32_t stage = 0, phase = 0, uidx = 0;
+            bool ok = true;
+            while (ok && it.next(p, u)) {
+                const uint32_t buf = uidx & 1;
+                const uint32_t use = uidx >> 1;
+                if (!mbar_wait(tempty_bar + 8 * buf, (use & 1) ^ 1, SITE_MMA_TMEM_EMPTY, abort_flag, wait_limit_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * BN;
+                for (uint32_t kb = u.k0; kb < u.k1; ++kb) {
+                    if (!mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = sbase + stage * L::SB;
+                    const uint32_t sb = sa + kABytes;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kTileK / 32; ++kk) {
+                        const uint64_t ad = umma_desc_sw128(sa + kk * a_step, a_lbo, 1024);
+                        const uint64_t bd = umma_desc_sw128(sb + kk * b_step, b_lbo, 1024);
+                        mma_i8(d_tmem, ad, bd, idesc, (kb > u.k0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(empty_bar + 8 * stage);
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+                if (!ok) break;
+                mma_commit(tfull_bar + 8 * buf);
+                ++uidx;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
+        const uint32_t row_local = q * 32 + lane;
+        const uint32_t ethread = threadIdx.x - 64;
+        UnitIter it;
+        it.init(p);
+        Unit u;
+        uint32_t uidx = 0;
+        bool ok = true;
+        while (ok && it.next(p, u)) {
+            const uint32_t buf = uidx & 1;
+            const uint32_t use = uidx >> 1;
+            if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t tm, tn;
+            tile_coords(p, u.tile, tm, tn);
+            const uint32_t row = tm * kTileM + row_local;
+            const uint32_t taddr = tmem_base + ((q * 32) << 16) + buf * BN;
+            const bool full = (u.k0 == 0 && u.k1 == p.k_blocks);
+            if (full) {
+#pragma unroll 1
+                for (uint32_t ch = 0; ch < NCH; ++ch) {
+                    int32_t acc[CW];
+                    tmem_ld_chunk<CW>(taddr + ch * CW, acc);
+                    tmem_ld_wait();
+                    if (ch == NCH - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
+                    }
+                    store_chunk<CW>(p, row, tn * BN + ch * CW, acc);
+                }
+            } else {
+                // Stream-K partial: accumulate into the workspace tile
+                // (column-major [BN][128] so a warp's adds are coalesced).
+                const uint32_t slot = u.tile - p.dp_tiles;
+                int32_t* wt = p.ws + (size_t)slot * (BN * kTileM);
+#pragma unroll 1
+                for (uint32_t ch = 0; ch < NCH; ++ch) {
+                    int32_t acc[CW];
+                    tmem_ld_chunk<CW>(taddr + ch * CW, acc);
+                    tmem_ld_wait();
+                    if (ch == NCH - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
+                    }
+#pragma unroll
+                    for (uint32_t j = 0; j < CW; ++j) atomicAdd(wt + (size_t)(ch * CW + j) * kTileM + row_local, acc[j]);
+                }
+                __threadfence();
+                named_bar_sync(1, kEpiThreads);
+                if (ethread == 0) {
+                    const uint32_t add = u.k1 - u.k0;
+                    const uint32_t old = atomicAdd(p.ws_cnt + slot, add);
+                    *epi_flag = (old + add == p.k_blocks) ? 1 : 0;
+                }
+                named_bar_sync(1, kEpiThreads);
+                if (*epi_flag) {
+                    // This contribution completed the tile: finish it and
+                    // leave the workspace zeroed for the next call.
+                    __threadfence();
+#pragma unroll 1
+                    for (uint32_t ch = 0; ch < NCH; ++ch) {
+                        int32_t acc[CW];
+#pragma unroll
+                        for (uint32_t j = 0; j < CW; ++j) {
+                            int32_t* w = wt + (size_t)(ch * CW + j) * kTileM + row_local;
+                            acc[j] = __ldcg(w);
+                            __stcg(w, 0);
+                        }
+                        store_chunk<CW>(p, row, tn * BN + ch * CW, acc);
+                    }
+                    if (ethread == 0) p.ws_cnt[slot] = 0;
+                }
+            }
+            ++uidx;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// --------------------------------------------------------------------------
+// Host side
+// --------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// 2-D int8 operand map.  K-major: dims {K, rows}; MN-major: dims {rows, K}.
+bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint32_t K, uint32_t ld, bool mn_major,
+                      uint32_t box_rows)
+{
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2];
+    cuuint32_t box[2];
+    if (mn_major) {
+        dims[0] = rows;
+        dims[1] = K;
+        box[0] = 128;
+        box[1] = kTileK;
+    } else {
+        dims[0] = K;
+        dims[1] = rows;
+        box[0] = kTileK;
+        box[1] = box_rows;
+    }
+    cuuint64_t strides[1] = {ld};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <uint32_t BN>
+cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
+{
+    using L = Smem<BN>;
+    // The shared-memory opt-in is a per-device function attribute.
+    static std::atomic<uint64_t> done_mask{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done_mask.load() & bit)) {
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+        if (e != cudaSuccess) return e;
+        done_mask.fetch_or(bit);
+    }
+    gemm_i8_kernel<BN><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_major, bool allow_stream_k,
+                        uint32_t num_sms, GemmSchedule& s)
+{
+    s = GemmSchedule{};
+    uint32_t bn = 16;
+    while (bn < Nk && bn < 256) bn <<= 1;
+    if (b_mn_major && bn < 128) bn = 128;  // MN-major B tiles are 128-element swizzle rows
+    s.tile_n = bn;
+    s.stages = num_stages(bn);
+    s.tiles_m = (Mk + kTileM - 1) / kTileM;
+    s.tiles_n = (Nk + bn - 1) / bn;
+    s.k_blocks = (K + kTileK - 1) / kTileK;
+    const uint64_t T = (uint64_t)s.tiles_m * s.tiles_n;
+    const uint32_t P = num_sms ? num_sms : 148;
+    if (!allow_stream_k || s.k_blocks < 2 || (T % P == 0)) {
+        s.dp_tiles = (uint32_t)T;
+        s.sk_iters = 0;
+        s.ctas = (uint32_t)(T < P ? T : P);
+    } else if (T >= 4ull * P) {
+        // Whole waves data-parallel, the partial last wave split by k-blocks.
+        s.dp_tiles = (uint32_t)((T / P) * P);
+        s.sk_iters = (T - s.dp_tiles) * (uint64_t)s.k_blocks;
+        s.ctas = P;
+    } else {
+        // Few waves: stream-K over everything keeps every SM busy to the end.
+        s.dp_tiles = 0;
+        s.sk_iters = T * (uint64_t)s.k_blocks;
+        s.ctas = (uint32_t)(s.sk_iters < P ? s.sk_iters : P);
+    }
+    const uint64_t tail = T - s.dp_tiles;
+    s.workspace_bytes = tail ? (size_t)(tail * (uint64_t)bn * kTileM * 4 + ((tail * 4 + 255) & ~255ull)) : 0;
+}
+
+cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* workspace, cudaStream_t st,
+                           const char** detail)
+{
+    const uint32_t bn = s.tile_n;
+    CUtensorMap ta, tb;
+    if (!make_operand_map(&ta, p.a, p.Mk, p.K, p.lda, p.a_mn_major != 0, kTileM) ||
+        !make_operand_map(&tb, p.b, p.Nk, p.K, p.ldb, p.b_mn_major != 0, bn)) {
+        if (detail) *detail = "cuTensorMapEncodeTiled rejected an operand (alignment / stride)";
+        return cudaErrorInvalidValue;
+    }
+    KParams kp{};
+    kp.Mk = p.Mk;
+    kp.Nk = p.Nk;
+    kp.K = p.K;
+    kp.tiles_m = s.tiles_m;
+    kp.tiles_n = s.tiles_n;
+    kp.k_blocks = s.k_blocks;
+    kp.dp_tiles = s.dp_tiles;
+    kp.ctas = s.ctas;
+    kp.sk_iters = s.sk_iters;
+    kp.a_mn_major = p.a_mn_major;
+    kp.b_mn_major = p.b_mn_major;
+    kp.c = p.c;
+    kp.ldc = p.ldc;
+    kp.c_type = p.c_type;
+    kp.transpose_out = p.transpose_out;
+    const uint32_t esz = p.c_type == 2 ? 4 : 2;
+    kp.vec_store_ok = ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0) && ((p.ldc * esz) % 16 == 0);
+    kp.row_scale_vec = p.row_scale_vec;
+    kp.col_scale_vec = p.col_scale_vec;
+    kp.row_scale = p.row_scale;
+    kp.col_scale = p.col_scale;
+    if (s.workspace_bytes) {
+        const uint64_t tail = (uint64_t)s.tiles_m * s.tiles_n - s.dp_tiles;
+        kp.ws = static_cast<int32_t*>(workspace);
+        kp.ws_cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + tail * bn * kTileM * 4);
+    }
+    kp.raster_group = 16;
+    if (kp.ctas == 0) return cudaSuccess;
+    switch (bn) {
+        case 16: return launch_bn<16>(ta, tb, kp, st);
+        case 32: return launch_bn<32>(ta, tb, kp, st);
+        case 64: return launch_bn<64>(ta, tb, kp, st);
+        case 128: return launch_bn<128>(ta, tb, kp, st);
+        case 256: return launch_bn<256>(ta, tb, kp, st);
+        default:
+            if (detail) *detail = "internal: unsupported tile_n";
+            return cudaErrorInvalidValue;
+    }
+}
+
+// --------------------------------------------------------------------------
+// Device status + debug bounded wait
+// --------------------------------------------------------------------------
+namespace {
+__global__ void debug_wait_kernel(uint64_t limit_ns)
+{
+    __shared__ alignas(8) uint64_t bar;
+    const uint32_t b = smem_u32(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(b, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // Nothing ever arrives on this barrier: the wait must give up.
+        mbar_wait(b, 0, SITE_DEBUG, nullptr, limit_ns);
+    }
+    __syncthreads();
+}
+}  // namespace
+
+cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st)
+{
+    debug_wait_kernel<<<1, 32, 0, st>>>(limit_ns);
+    return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value)
+{
+    uint32_t v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return e;
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return e;
+    if (v != 0) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    *value = v;
+    return e;
+}
+
+}  // namespace b2sq

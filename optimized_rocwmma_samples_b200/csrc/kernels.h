@@ -1,0 +1,65 @@
+// kernels.h — internal launch interface between the C ABI (api.cu) and the
+// kernel translation units.  Not installed; the public surface is b2sq.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace b2sq {
+
+cudaError_t launch_smoothquant(const void* x, const float* s, int8_t* y, float* rs, uint32_t M, uint32_t N,
+                               float qmax, cudaStream_t st, int* used_vector_path);
+
+cudaError_t launch_moe_smoothquant(const void* x, const float* s, const int32_t* ids, int8_t* qy, float* rs,
+                                   uint32_t T, uint32_t H, uint32_t K, uint32_t E, float qmax,
+                                   const int32_t* perm, cudaStream_t st, int* used_vector_path);
+
+// GEMM problem after the host has mapped the user's (A, B, layouts) onto the
+// kernel's operands: kernel A has Mk rows, kernel B has Nk rows, both K long.
+struct GemmProblem {
+    uint32_t Mk, Nk, K;
+    const int8_t* a;  // kernel A operand
+    uint32_t a_mn_major, lda;
+    const int8_t* b;  // kernel B operand
+    uint32_t b_mn_major, ldb;
+    void* c;
+    uint32_t ldc;
+    int c_type;         // 0 f16, 1 bf16, 2 i32
+    int transpose_out;  // 1: element (i, j) of the kernel result goes to c[j * ldc + i]
+    const float* row_scale_vec;  // per kernel-row scale (nullable)
+    const float* col_scale_vec;  // per kernel-column scale (nullable)
+    float row_scale, col_scale;  // used when the vector is null
+};
+
+struct GemmSchedule {
+    uint32_t swap_ab;
+    uint32_t tile_n;
+    uint32_t stages;
+    uint32_t tiles_m, tiles_n, k_blocks;
+    uint32_t ctas;
+    uint32_t dp_tiles;
+    uint64_t sk_iters;
+    size_t workspace_bytes;  // bytes of workspace the schedule needs (0 without stream-K)
+};
+
+constexpr uint32_t kTileM = 128;
+constexpr uint32_t kTileK = 128;
+
+// Chooses tile_n, stages and the persistent/stream-K split (host only).
+void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_major, bool allow_stream_k,
+                        uint32_t num_sms, GemmSchedule& s);
+
+// Launches the tcgen05 GEMM.  workspace may be null only if
+// s.workspace_bytes == 0.  Returns a CUDA error or cudaSuccess; *detail gets
+// a static explanation on failure.
+cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* workspace, cudaStream_t st,
+                           const char** detail);
+
+// Debug: a kernel that waits for an mbarrier nobody arrives on, with a limit.
+cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st);
+
+// Device status word access.
+cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value);
+
+}  // namespace b2sq

@@ -1,0 +1,126 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the header
+declares, validates arguments before touching CUDA, and its scheduler covers
+every (tile, k-block) exactly once.  No GPU needed."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from optimized_rocwmma_samples_b200 import _lib, api
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "b2sq.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"B2SQ_API\s+[\w\s\*]+?\b(b2sq_\w+)\s*\(", text)))
+
+
+def test_header_symbols_exported():
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert len(syms) >= 10
+    for s in syms:
+        assert hasattr(lib, s), s
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+
+
+def test_version_and_strings():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.b2sq_version()
+    assert lib.b2sq_status_string(0) == b"ok"
+    assert lib.b2sq_status_string(4) == b"device wait timed out"
+
+
+def test_gemm_argument_validation_without_gpu():
+    lib = _lib.load()
+    ok = lib.b2sq_gemm_i8(0, 16, 16, None, 0, 16, None, 1, 16, None, 1, 16, None, None, 1.0, 1.0, None, 0, None)
+    assert ok == _lib.B2SQ_OK  # empty problem: no-op
+    buf = (C.c_int8 * 64)()
+    addr = C.addressof(buf)
+    # bad layout
+    assert lib.b2sq_gemm_i8(16, 16, 16, addr, 7, 16, addr, 1, 16, addr, 1, 16, None, None, 1, 1, None, 0,
+                            None) == _lib.B2SQ_ERR_INVALID_ARG
+    # bad dtype
+    assert lib.b2sq_gemm_i8(16, 16, 16, addr, 0, 16, addr, 1, 16, addr, 9, 16, None, None, 1, 1, None, 0,
+                            None) == _lib.B2SQ_ERR_INVALID_ARG
+    # null output
+    assert lib.b2sq_gemm_i8(16, 16, 16, addr, 0, 16, addr, 1, 16, None, 1, 16, None, None, 1, 1, None, 0,
+                            None) == _lib.B2SQ_ERR_INVALID_ARG
+    # ldc < n
+    assert lib.b2sq_gemm_i8(16, 16, 16, addr, 0, 16, addr, 1, 16, addr, 1, 8, None, None, 1, 1, None, 0,
+                            None) == _lib.B2SQ_ERR_INVALID_ARG
+    # lda < k
+    assert lib.b2sq_gemm_i8(16, 16, 32, addr, 0, 16, addr, 1, 32, addr, 1, 16, None, None, 1, 1, None, 0,
+                            None) == _lib.B2SQ_ERR_INVALID_ARG
+    # lda not a multiple of 16 -> unsupported (TMA)
+    aligned = (addr + 15) & ~15
+    assert lib.b2sq_gemm_i8(16, 16, 20, aligned, 0, 24, aligned, 1, 32, aligned, 1, 16, None, None, 1, 1, None, 0,
+                            None) == _lib.B2SQ_ERR_UNSUPPORTED
+    assert b"multiples of 16" in lib.b2sq_last_error_message()
+    # misaligned operand -> unsupported
+    assert lib.b2sq_gemm_i8(16, 16, 16, aligned + 1, 0, 16, aligned, 1, 16, aligned, 1, 16, None, None, 1, 1,
+                            None, 0, None) == _lib.B2SQ_ERR_UNSUPPORTED
+
+
+def test_smoothquant_argument_validation_without_gpu():
+    lib = _lib.load()
+    buf = (C.c_float * 16)()
+    p = C.addressof(buf)
+    assert lib.b2sq_smoothquant(p, p, p, p, 4, 4, 0.0, None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_smoothquant(p, p, p, p, 4, 4, float("nan"), None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_smoothquant(p, p, p, p, 0, 4, 127.0, None) == _lib.B2SQ_OK
+    assert lib.b2sq_smoothquant(None, p, p, p, 4, 4, 127.0, None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_moe_smoothquant(p, p, None, p, p, 4, 4, 2, 8, 127.0, None, None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_moe_smoothquant(p, p, p, p, p, 0, 4, 2, 8, 127.0, None, None) == _lib.B2SQ_OK
+    assert lib.b2sq_debug_bounded_wait(0, None) == _lib.B2SQ_ERR_INVALID_ARG
+
+
+def simulate_units(pl):
+    """Host restatement of the kernel's per-CTA work list (UnitIter in gemm_i8.cu)."""
+    T = pl.tiles_m * pl.tiles_n
+    kb = pl.k_blocks
+    cover = {}
+    for cta in range(pl.ctas):
+        t = cta
+        while t < pl.dp_tiles:
+            cover.setdefault(t, []).append((0, kb))
+            t += pl.ctas
+        pos = cta * pl.sk_iters // pl.ctas
+        end = (cta + 1) * pl.sk_iters // pl.ctas
+        while pos < end:
+            tt, k0 = divmod(pos, kb)
+            k1 = min(kb, k0 + (end - pos))
+            cover.setdefault(pl.dp_tiles + tt, []).append((k0, k1))
+            pos += k1 - k0
+    return T, kb, cover
+
+
+@pytest.mark.parametrize("m,n,k", [(8192, 8192, 8192), (16, 28672, 8192), (64, 28672, 8192),
+                                   (16384, 28672, 8192), (19 * 128, 20 * 256, 1024), (1, 16, 16),
+                                   (3000, 3000, 3000), (128, 128, 128 * 1000)])
+@pytest.mark.parametrize("sk", [True, False])
+def test_schedule_covers_each_kblock_once(m, n, k, sk):
+    pl = api.plan(m, n, k, api.ROW_MAJOR, api.COL_MAJOR, use_stream_k=sk, num_sms=148)
+    assert pl.ctas <= 148
+    T, kb, cover = simulate_units(pl)
+    assert set(cover) == set(range(T))
+    for t, ranges in cover.items():
+        ranges.sort()
+        pos = 0
+        for k0, k1 in ranges:
+            assert k0 == pos and k1 > k0
+            pos = k1
+        assert pos == kb
+
+
+def test_plan_choices():
+    p = api.plan(16, 28672, 8192, num_sms=148)
+    assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 0  # all stream-K
+    p = api.plan(8192, 8192, 8192, num_sms=148)
+    assert p.swap_ab == 0 and p.tile_n == 256 and p.tiles_m * p.tiles_n == 2048
+    assert p.dp_tiles == 13 * 148 and p.sk_iters == (2048 - 13 * 148) * 64
+    p = api.plan(8192, 8192, 8192, api.ROW_MAJOR, api.ROW_MAJOR, num_sms=148)
+    assert p.tile_n in (128, 256)

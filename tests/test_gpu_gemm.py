@@ -1,0 +1,185 @@
+"""GPU parity of the tcgen05 int8 GEMM: int32 accumulators bit-exact against
+the oracle (exact integer arithmetic), fp16/bf16 dequantised outputs within
+1 ulp of the oracle's fp32 epilogue rounded to the output type (in practice
+bit-exact: both compute cvt_rn(float(acc) * (sa * sb)) in fp32)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from optimized_rocwmma_samples_b200 import api, synth
+
+pytestmark = pytest.mark.gpu
+
+ULP_TOL = 1  # north-star tolerance for fp16/bf16 outputs
+
+
+def to_dev(arr: np.ndarray, major: str, pad: int = 0) -> torch.Tensor:
+    """Logical [R, C] int8 array as a device view with the requested memory order
+    and a leading dimension rounded up to 16 (+pad)."""
+    dev = torch.device("cuda", 0)
+    R, C = arr.shape
+    t = torch.from_numpy(np.ascontiguousarray(arr))
+    if major == "row":
+        ld = ((C + 15) // 16) * 16 + pad
+        buf = torch.zeros((max(R, 1), ld), dtype=torch.int8, device=dev)
+        buf[:R, :C] = t.to(dev)
+        return buf[:R, :C]
+    ld = ((R + 15) // 16) * 16 + pad
+    buf = torch.zeros((max(C, 1), ld), dtype=torch.int8, device=dev)
+    buf[:C, :R] = t.t().contiguous().to(dev)
+    return buf[:C, :R].t()
+
+
+def ulp_dist(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    def ordinal(b):
+        b = b.astype(np.int32)
+        return np.where(b & 0x8000, -(b & 0x7FFF), b)
+
+    return np.abs(ordinal(a_bits) - ordinal(b_bits))
+
+
+def run_case(M, N, K, la="row", lb="col", out="bf16", stream_k=True, pad=0, vec_scales=True, seed=0):
+    rng = np.random.default_rng(seed + M * 31 + N * 7 + K)
+    a = synth.weights_np(rng, M, K)
+    b = synth.weights_np(rng, K, N)
+    sa = synth.scales_np(rng, M)
+    sb = synth.scales_np(rng, N)
+    dev = torch.device("cuda", 0)
+    ta, tb = to_dev(a, la, pad), to_dev(b, lb, pad)
+    acc_ref = O.gemm_i8_acc(a, b)
+    c32 = api.gemm_quant(ta, tb, out_dtype=torch.int32, stream_k=stream_k)
+    torch.cuda.synchronize()
+    got = c32.cpu().numpy()
+    bad = np.argwhere(got != acc_ref)
+    assert bad.size == 0, f"int32 mismatch at {bad[:5].tolist()} ({len(bad)} total)"
+    if out == "i32":
+        return
+    dt = torch.float16 if out == "f16" else torch.bfloat16
+    if vec_scales:
+        c = api.gemm_quant(ta, tb, torch.from_numpy(sa).to(dev), torch.from_numpy(sb).to(dev), out_dtype=dt,
+                           stream_k=stream_k)
+        ref = O.dequant(acc_ref, sa, sb, out_dtype=out)
+    else:  # tensor-scale mode of the reference (scale_a = scale_b = 1/127, :227)
+        c = api.gemm_quant(ta, tb, scale_a=1 / 127, scale_b=1 / 127, out_dtype=dt, stream_k=stream_k)
+        ref = O.dequant(acc_ref, None, None, np.float32(1 / 127), np.float32(1 / 127), out_dtype=out)
+    torch.cuda.synchronize()
+    bits = c.view(torch.int16).cpu().numpy().view(np.uint16)
+    assert ulp_dist(bits, ref).max() <= ULP_TOL
+    assert np.array_equal(bits, ref)  # stronger: identical fp32 epilogue
+
+
+LAYOUTS = [("row", "col"), ("row", "row"), ("col", "col"), ("col", "row")]
+
+
+@pytest.mark.parametrize("la,lb", LAYOUTS)
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (130, 200, 304), (384, 768, 2048), (1, 300, 64)])
+def test_layouts_shapes(cuda_device, la, lb, M, N, K):
+    run_case(M, N, K, la, lb)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 2048, 1024), (64, 4096, 512), (1, 1024, 256), (100, 640, 4096),
+                                   (33, 28672, 256)])
+def test_skinny_m_swap(cuda_device, M, N, K):
+    run_case(M, N, K, "row", "col", out="f16")
+
+
+@pytest.mark.parametrize("M,N,K", [(1000, 1000, 1000), (129, 257, 1040), (517, 95, 333)])
+def test_ragged_padded(cuda_device, M, N, K):
+    run_case(M, N, K, "row", "col", pad=16)
+    run_case(M, N, K, "col", "row", pad=32, out="f16")
+
+
+@pytest.mark.parametrize("stream_k", [True, False])
+def test_stream_k_equivalence(cuda_device, stream_k):
+    # 148 SMs, 128x256 tiles: 19 x 20 = 380 tiles -> 2 full waves + stream-K tail
+    run_case(19 * 128, 20 * 256, 1024, stream_k=stream_k)
+
+
+def test_stream_k_workspace_reuse(cuda_device):
+    # repeated calls reuse the same workspace; it must come back zeroed
+    for i in range(3):
+        run_case(16, 28672, 1024, out="f16", seed=i)
+
+
+def test_tensor_scale_mode(cuda_device):
+    run_case(256, 256, 512, out="f16", vec_scales=False)
+
+
+def test_k_zero_and_empty(cuda_device):
+    dev = cuda_device
+    a = torch.zeros((4, 0), dtype=torch.int8, device=dev)
+    b = torch.zeros((0, 8), dtype=torch.int8, device=dev)
+    c = torch.full((4, 8), 3.0, dtype=torch.bfloat16, device=dev)
+    api.gemm_quant(a, b, c=c)
+    torch.cuda.synchronize()
+    assert torch.all(c == 0)
+
+
+def test_c1_chain_golden(cuda_device):
+    """smoothquant -> GEMM on the CPU-runnable configuration against the fixture."""
+    from golden.make_golden import GOLDEN
+
+    g = np.load(GOLDEN)
+    dev = cuda_device
+    y, rs = api.smoothquant(torch.from_numpy(g["x"]).to(dev), torch.from_numpy(g["smooth"]).to(dev))
+    w = torch.from_numpy(g["w_nk"]).to(dev)  # [N, K] K-major -> B = w.t()
+    acc = api.gemm_quant(y, w.t(), out_dtype=torch.int32)
+    out = api.gemm_quant(y, w.t(), rs, torch.from_numpy(g["sb"]).to(dev), out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    assert np.array_equal(acc.cpu().numpy(), g["acc"])
+    assert np.array_equal(out.view(torch.int16).cpu().numpy().view(np.uint16), g["out_f16"])
+
+
+def test_full_size_square_8192(cuda_device):
+    """C2: 8192^3, A row-major, B column-major, bf16 out.  Whole int32 result
+    checked against cuBLASLt's exact int8 GEMM; sampled rows against the oracle."""
+    dev = cuda_device
+    n = 8192
+    a = synth.torch_int8_uniform((n, n), dev, 11)
+    w = synth.torch_int8_uniform((n, n), dev, 12)  # [N, K]
+    b = w.t()
+    c32 = api.gemm_quant(a, b, out_dtype=torch.int32)
+    ref = torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(c32, ref)
+    rows = torch.arange(0, n, 509, device=dev)
+    acc0 = O.gemm_i8_acc(a[rows].cpu().numpy(), w.cpu().numpy().T)
+    assert np.array_equal(c32[rows].cpu().numpy(), acc0)
+    sa = synth.torch_scales(n, dev, 13)
+    sb = synth.torch_scales(n, dev, 14)
+    c = api.gemm_quant(a, b, sa, sb, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    ref_bits = O.dequant(acc0, sa[rows].cpu().numpy(), sb.cpu().numpy(), out_dtype="bf16")
+    assert np.array_equal(c[rows].view(torch.int16).cpu().numpy().view(np.uint16), ref_bits)
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_full_size_decode(cuda_device, M):
+    """C3: [M, 8192] x [8192, 28672] (K-major weights), fp16 out, whole output vs oracle."""
+    dev = cuda_device
+    rng = np.random.default_rng(M)
+    a = synth.weights_np(rng, M, 8192)
+    w = synth.torch_int8_uniform((28672, 8192), dev, 21)
+    sa = synth.scales_np(rng, M)
+    sb = synth.torch_scales(28672, dev, 22)
+    ta = torch.from_numpy(a).to(dev)
+    c32 = api.gemm_quant(ta, w.t(), out_dtype=torch.int32)
+    c = api.gemm_quant(ta, w.t(), torch.from_numpy(sa).to(dev), sb, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    acc0 = O.gemm_i8_acc(a, w.cpu().numpy().T)
+    assert np.array_equal(c32.cpu().numpy(), acc0)
+    assert np.array_equal(c.view(torch.int16).cpu().numpy().view(np.uint16),
+                          O.dequant(acc0, sa, sb.cpu().numpy(), out_dtype="f16"))
+
+
+def test_no_device_timeout_flag(cuda_device):
+    run_case(256, 512, 1024)
+    assert api.last_device_error() == 0
+
+
+def test_bounded_wait_reports_timeout(cuda_device):
+    # a wait nothing satisfies gives up after 2 ms and reports TIMEOUT; the context stays usable
+    st = api.debug_bounded_wait(2000)
+    assert st == 4  # B2SQ_ERR_TIMEOUT
+    run_case(128, 256, 256)
