@@ -1,0 +1,368 @@
+"""Benchmark of the smoothquant -> int8 GEMM hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload: int8 GEMM M = N = K = 8192, A row-major,
+B column-major (K-major weights), per-row x per-column fp32 dequant, bf16 out.
+One step = one b2sq_gemm_i8 call.  ``value`` is whole-job TOPS (2*M*N*K per
+step per rank) with inputs resident in HBM; L2 (126 MB) is flushed by writing
+a 512 MB buffer before every timed step, outside the timed events.
+At N > 1 GPUs the GEMM is N-sharded (column-parallel weights, weak scaling:
+every rank owns an 8192-column weight shard and the same activations), the
+output stays N-sharded; there is no collective inside the timed step.
+
+Extra objects on the JSON line:
+  roofline      the GEMM kernel against the int8 dense peak derived from the
+                measured bf16 peak (2x, MEASURED_PEAKS.json)
+  smoothquant   GB/s of b2sq_smoothquant at the prefill activation shape
+                16384 x 8192 (reference byte formula, rocwmma_smoothquant.cpp:157-158)
+  e2e           the same GEMM through the C ABI from pinned host buffers:
+                H2D of A, B and scales + GEMM + D2H of C inside the timed region
+  cpu_baseline  the CPU oracle (restated reference CPU path) on a row sample
+
+``--impl reference`` times the reference's CPU path (the oracle restatement;
+the HIP reference cannot run on this machine) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+M = N = K = 8192
+FLUSH_BYTES = 512 << 20
+SQ_M, SQ_K = 16384, 8192
+
+# DRAM bytes (read + write) of one gemm_i8_kernel<256> launch at 8192^3, from
+# the ncu capture summarised in profiles/gemm_i8_8192_ncu.md (null until captured).
+GEMM_TRAFFIC_BYTES = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64"], default=None,
+                    help="run 3 launches of one kernel on its workload and exit (for ncu captures)")
+    return ap.parse_args()
+
+
+def run_profile(kind: str):
+    """Three launches of one kernel at its workload size, nothing else (ncu target)."""
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    from optimized_rocwmma_samples_b200 import api, synth
+
+    dev = torch.device("cuda", 0)
+    if kind == "smoothquant":
+        x = torch.randn((SQ_M, SQ_K), device=dev).to(torch.float16)
+        s = torch.ones((SQ_K,), device=dev)
+        for _ in range(3):
+            api.smoothquant(x, s)
+    else:
+        m = {"gemm": M, "decode16": 16, "decode64": 64}[kind]
+        n = N if kind == "gemm" else 28672
+        a = synth.torch_int8_uniform((m, K), dev, 1)
+        w = synth.torch_int8_uniform((n, K), dev, 2)
+        sa, sb = synth.torch_scales(m, dev, 3), synth.torch_scales(n, dev, 4)
+        dt = torch.bfloat16 if kind == "gemm" else torch.float16
+        for _ in range(3):
+            api.gemm_quant(a, w.t(), sa, sb, out_dtype=dt)
+    torch.cuda.synchronize()
+    print(f"profile {kind}: 3 launches done")
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and throttle reasons every 20 ms on a thread."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, local_rank: int):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[local_rank]) if vis else local_rank
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._nv = pynvml
+        except Exception:  # NVML unavailable: clocks reported as null
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- CPU oracle
+def cpu_gemm_sample(budget_s: float, seed: int = 0):
+    """Times the oracle's int8 GEMM (+ dequant) on a row sample of the 8192^3
+    workload; returns (TOPS, rows, seconds, threads)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    rng = np.random.default_rng(seed)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)  # [N, K] K-major
+    sb = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    rows = 4
+    while True:
+        a = rng.integers(-127, 128, size=(rows, K), dtype=np.int8)
+        sa = rng.uniform(1e-3, 1e-2, rows).astype(np.float32)
+        t0 = time.perf_counter()
+        O.gemm_quant(a, w.T, sa, sb, out_dtype="bf16")
+        dt = time.perf_counter() - t0
+        if dt >= budget_s * 0.5 or rows >= M:
+            return 2.0 * rows * N * K / dt / 1e12, rows, dt, O.num_threads()
+        rows = min(M, max(rows * 2, int(rows * budget_s / max(dt, 1e-3))))
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    total_steps = args.steps + args.warmup
+    per_step = max(0.5, min(3.0, 150.0 / max(total_steps, 1)))
+    times, rows_used, thr = [], 0, 1
+    for i in range(total_steps):
+        tops, rows, dt, thr = cpu_gemm_sample(per_step, seed=i)
+        if i >= args.warmup:
+            times.append(tops)
+            rows_used = rows
+    value = statistics.median(times)
+    sample = f"{rows_used} of {M} rows of the {M}x{N}x{K} int8 GEMM + bf16 dequant per step, oracle (gcc -O3 OpenMP)"
+    line = {
+        "impl": "reference", "metric": "int8 GEMM TOPS at 8192^3 (M=N=K=8192, bf16 out)", "value": value,
+        "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8->int32",
+        "data": "synthetic", "config": {"workload": "c2_square_int8_gemm_8192", "M": M, "N": N, "K": K,
+                                         "parallelism": "cpu-reference"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": thr, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is HIP/rocWMMA (AMD only): its CPU path is restated in oracle/ and timed here",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if args.profile:
+        return run_profile(args.profile)
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from optimized_rocwmma_samples_b200 import api, synth
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    hbm_gbs, bf16_tflops, peak_src = measured_peaks()
+    int8_peak = 2.0 * bf16_tflops
+
+    # inputs: same activations on every rank, a distinct weight shard per rank
+    a = synth.torch_int8_uniform((M, K), dev, 11)
+    w = synth.torch_int8_uniform((N, K), dev, 100 + rank)  # [N_shard, K] K-major
+    b = w.t()
+    sa = synth.torch_scales(M, dev, 13)
+    sb = synth.torch_scales(N, dev, 200 + rank)
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ws = api.Workspace()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        api.gemm_quant(a, b, sa, sb, out_dtype=torch.bfloat16, c=c, workspace=ws)
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        t_wall = time.perf_counter()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+    barrier()
+    if api.last_device_error() != 0:
+        raise RuntimeError("a bounded device wait timed out during the benchmark")
+    step_ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+    ms = statistics.mean(step_ms)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ops = 2.0 * M * N * K
+    value = world * ops / (ms_max * 1e-3) / 1e12
+    achieved = ops / (ms * 1e-3) / 1e12
+
+    # ---------------- smoothquant at the prefill activation shape (HBM bound)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    x = torch.randn((SQ_M, SQ_K), generator=g, device=dev).to(torch.float16)
+    s = torch.empty((SQ_K,), device=dev).uniform_(0.5, 2.0, generator=g)
+    y = torch.empty((SQ_M, SQ_K), dtype=torch.int8, device=dev)
+    rs = torch.empty((SQ_M,), dtype=torch.float32, device=dev)
+    for _ in range(5):
+        api.smoothquant(x, s, y=y, row_scale=rs)
+    sq_ms = []
+    for _ in range(50):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        api.smoothquant(x, s, y=y, row_scale=rs)
+        e1.record(stream)
+        sq_ms.append((e0, e1))
+    torch.cuda.synchronize()
+    sq_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in sq_ms)
+    sq_bytes = SQ_M * SQ_K * 2 + SQ_M * SQ_K + SQ_K * 4 + SQ_M * 4
+    sq_gbs = sq_bytes / (sq_ms * 1e-3) / 1e9
+    del x, y
+
+    # ---------------- e2e through the C ABI from pinned host buffers
+    h_a = a.cpu().pin_memory()
+    h_w = w.cpu().pin_memory()
+    h_sa = sa.cpu().pin_memory()
+    h_sb = sb.cpu().pin_memory()
+    h_c = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    d_a, d_w = torch.empty_like(a), torch.empty_like(w)
+    d_sa, d_sb = torch.empty_like(sa), torch.empty_like(sb)
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        d_a.copy_(h_a, non_blocking=True)
+        d_w.copy_(h_w, non_blocking=True)
+        d_sa.copy_(h_sa, non_blocking=True)
+        d_sb.copy_(h_sb, non_blocking=True)
+        api.gemm_quant(d_a, d_w.t(), d_sa, d_sb, out_dtype=torch.bfloat16, c=c, workspace=ws)
+        h_c.copy_(c, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * ops / (float(t.item()) * 1e-3) / 1e12
+    h2d = a.numel() + w.numel() + 4 * (sa.numel() + sb.numel())
+    d2h = c.numel() * 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tops, rows, dt, thr = cpu_gemm_sample(10.0)
+        cpu = {"value": tops, "unit": "TOPS", "cores": thr, "kind": "port",
+               "sample": f"{rows} of {M} rows of the 8192^3 int8 GEMM + bf16 dequant ({dt:.1f} s), "
+                         "oracle restating the reference CPU path (gcc -O3, OpenMP)"}
+
+    if rank == 0:
+        line = {
+            "metric": "int8 GEMM TOPS at 8192^3 (M=N=K=8192, bf16 out)",
+            "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8->int32", "data": "synthetic",
+            "config": {"workload": "c2_square_int8_gemm_8192", "M": M, "N": N, "K": K,
+                       "a_layout": "row-major", "b_layout": "column-major (K-major weights)",
+                       "scales": "per-row x per-column fp32", "out": "bf16",
+                       "parallelism": f"n-sharded x{world}" if world > 1 else "single-gpu",
+                       "l2": "flushed (512 MB write) before every timed step"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                         "frac": achieved / int8_peak, "traffic": GEMM_TRAFFIC_BYTES,
+                         "peak_note": f"2 x {peak_src} bf16 dense {bf16_tflops} TFLOP/s (int8 dense rate = 2x bf16); "
+                                      f"nominal int8 4500 TOPS -> frac {achieved / 4500.0:.3f}"},
+            "smoothquant": {"shape": [SQ_M, SQ_K], "ms": sq_ms, "gbs": sq_gbs,
+                            "frac_of_measured_hbm": sq_gbs / hbm_gbs, "hbm_peak_gbs": hbm_gbs},
+            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "wall_s_timed": t_wall,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
