@@ -116,11 +116,14 @@ B2SQ_API b2sq_status b2sq_moe_smoothquant(const void* x_f16, const float* smooth
  * Requirements (else UNSUPPORTED): a, b 16-byte aligned, lda and ldb
  * multiples of 16.  M, N, K need not be tile multiples.
  *
- * workspace: optional int32 scratch for stream-K splitting of tiles across
- * SMs.  Query its size with b2sq_gemm_i8_workspace_size.  It must be zero
- * filled before its first use; every completed call leaves it zero filled
- * again.  NULL (or too small) disables stream-K; results are identical either
- * way (int32 sums are exact and order independent).
+ * workspace: optional scratch for stream-K splitting of tiles across SMs
+ * (per-CTA int32 partial tiles + per-tile counters).  Query its size with
+ * b2sq_gemm_i8_workspace_size; it must be 256-byte aligned and zero filled
+ * before its first use; every completed call leaves its counters zero again,
+ * so it can be reused without clearing by stream-ordered calls (concurrent
+ * calls need separate workspaces).  NULL (or too small) disables stream-K;
+ * results are identical either way (int32 sums are exact and order
+ * independent).
  */
 B2SQ_API b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k,
                          const int8_t* a, b2sq_layout la, uint32_t lda,

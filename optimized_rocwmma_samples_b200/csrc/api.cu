@@ -194,7 +194,7 @@ b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k, b2sq_layout la
     plan->swap_ab = mp.swap;
     plan->tile_m = b2sq::kTileM;
     plan->tile_n = s.tile_n;
-    plan->tile_k = b2sq::kTileK;
+    plan->tile_k = s.tile_k;
     plan->stages = s.stages;
     plan->tiles_m = s.tiles_m;
     plan->tiles_n = s.tiles_n;

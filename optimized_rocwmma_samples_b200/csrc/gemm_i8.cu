@@ -18,13 +18,17 @@
 //                  cvt.rn to fp16/bf16, stores.  Two TMEM accumulators
 //                  alternate so the epilogue of tile i overlaps the main loop
 //                  of tile i+1.
-//  * tile schedule: whole tiles in data-parallel rounds over the CTAs, then
-//    the tail tiles' k-blocks split evenly over all CTAs (stream-K, the
-//    scheme of rocwmma_streamk_gemm.cpp:102-143).  Partial sums are added
-//    with int32 atomics into a workspace (exact, so the result does not
-//    depend on the split); the CTA whose contribution completes a tile's K
-//    range does its epilogue and re-zeroes the workspace.  No CTA ever waits
-//    on another CTA, so the fix-up cannot hang.
+//  * a stage holds BK elements of K: 128 for square tiles, up to 512 for the
+//    skinny (decode) tiles so every weight row is streamed in >= 256-byte
+//    runs per stage.
+//  * tile schedule: whole tiles in data-parallel rounds over the CTAs; when
+//    the last round would leave many SMs idle, the tail tiles' k-blocks are
+//    instead split evenly over all CTAs (stream-K, the scheme of
+//    rocwmma_streamk_gemm.cpp:102-143).  A CTA stores each partial tile to
+//    its own workspace slot (plain coalesced stores), then bumps the tile's
+//    k-block counter; the CTA whose contribution completes the tile sums the
+//    contributors' slots (int32, exact, order independent) and runs the
+//    epilogue.  No CTA ever waits on another CTA, so the fix-up cannot hang.
 //  * no TMA multicast anywhere (every CTA loads its own tiles).
 #include "common.cuh"
 #include "kernels.h"
@@ -37,20 +41,33 @@
 
 namespace b2sq {
 
+// Optional per-CTA timeline for experiments (compiled only with -DB2SQ_TRACE).
+#ifdef B2SQ_TRACE
+__device__ unsigned long long g_trace[4096 * 8];
+#define B2SQ_TRACE_POINT(i) (g_trace[blockIdx.x * 8 + (i)] = globaltimer_ns())
+#else
+#define B2SQ_TRACE_POINT(i) ((void)0)
+#endif
+
 namespace {
+
+#ifndef B2SQ_RASTER_GROUP
+#define B2SQ_RASTER_GROUP 16  // M tiles per raster group
+#endif
 
 constexpr uint32_t kThreads = 192;  // 6 warps
 constexpr uint32_t kEpiThreads = 128;
-constexpr uint32_t kABytes = kTileM * kTileK;  // 16 KiB per stage
-constexpr uint32_t kSmemBudget = 232448;       // 227 KiB opt-in limit per CTA
+constexpr uint32_t kSmemBudget = 232448;  // 227 KiB opt-in limit per CTA
 constexpr uint32_t kBarrierBytes = 256;
 
-__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn) { return kABytes + bn * kTileK; }
-__host__ __device__ constexpr uint32_t num_stages(uint32_t bn)
+// K depth of a pipeline stage for a tile width.
+__host__ __device__ constexpr uint32_t tile_k_for(uint32_t bn) { return bn <= 32 ? 512 : bn <= 64 ? 256 : 128; }
+__host__ __device__ constexpr uint32_t stage_bytes(uint32_t bn, uint32_t bk) { return (kTileM + bn) * bk; }
+__host__ __device__ constexpr uint32_t num_stages(uint32_t bn, uint32_t bk)
 {
-    return ((kSmemBudget - 1024 - kBarrierBytes) / stage_bytes(bn)) > 8
+    return ((kSmemBudget - 1024 - kBarrierBytes) / stage_bytes(bn, bk)) > 8
                ? 8
-               : ((kSmemBudget - 1024 - kBarrierBytes) / stage_bytes(bn));
+               : ((kSmemBudget - 1024 - kBarrierBytes) / stage_bytes(bn, bk));
 }
 __host__ __device__ constexpr uint32_t tmem_cols(uint32_t bn)
 {
@@ -71,31 +88,34 @@ struct KParams {
     const float* row_scale_vec;
     const float* col_scale_vec;
     float row_scale, col_scale;
-    int32_t* ws;        // [tail tiles][tile_n][128] int32
-    uint32_t* ws_cnt;   // [tail tiles] k-blocks accumulated so far
+    uint32_t* ws_cnt;   // [tail tiles] k-blocks accumulated so far (zero between calls)
+    int32_t* ws_slots;  // [ctas][2][tile_n][128] int32 partial tiles (scratch)
     uint32_t raster_group;
 };
 
 struct Unit {
     uint32_t tile, k0, k1;
+    uint32_t slot;  // 0: first stream-K unit of this CTA, 1: a later one
 };
+
+__host__ __device__ __forceinline__ uint64_t sk_start(uint64_t c, uint64_t S, uint64_t P) { return c * S / P; }
 
 // Work list of one CTA: its data-parallel tiles, then its contiguous range of
 // stream-K k-block iterations over the tail tiles.
 struct UnitIter {
     uint32_t dp_next;
-    uint64_t sk_pos, sk_end;
+    uint64_t sk_pos, sk_begin, sk_end;
 
     __device__ __forceinline__ void init(const KParams& p)
     {
         dp_next = blockIdx.x;
-        sk_pos = (uint64_t)blockIdx.x * p.sk_iters / p.ctas;
-        sk_end = (uint64_t)(blockIdx.x + 1) * p.sk_iters / p.ctas;
+        sk_begin = sk_pos = sk_start(blockIdx.x, p.sk_iters, p.ctas);
+        sk_end = sk_start(blockIdx.x + 1, p.sk_iters, p.ctas);
     }
     __device__ __forceinline__ bool next(const KParams& p, Unit& u)
     {
         if (dp_next < p.dp_tiles) {
-            u = {dp_next, 0, p.k_blocks};
+            u = {dp_next, 0, p.k_blocks, 0};
             dp_next += p.ctas;
             return true;
         }
@@ -104,7 +124,7 @@ struct UnitIter {
             const uint32_t k0 = (uint32_t)(sk_pos - t * p.k_blocks);
             const uint64_t rem = sk_end - sk_pos;
             const uint32_t k1 = (uint32_t)((k0 + rem < p.k_blocks) ? k0 + rem : p.k_blocks);
-            u = {p.dp_tiles + (uint32_t)t, k0, k1};
+            u = {p.dp_tiles + (uint32_t)t, k0, k1, sk_pos == sk_begin ? 0u : 1u};
             sk_pos += k1 - k0;
             return true;
         }
@@ -125,12 +145,12 @@ __device__ __forceinline__ void tile_coords(const KParams& p, uint32_t t, uint32
     tn = r / gsize;
 }
 
-template <uint32_t BN>
+template <uint32_t BN, uint32_t BK>
 struct Smem {
-    static constexpr uint32_t ST = num_stages(BN);
-    static constexpr uint32_t SB = stage_bytes(BN);
+    static constexpr uint32_t ST = num_stages(BN, BK);
+    static constexpr uint32_t A_BYTES = kTileM * BK;
+    static constexpr uint32_t SB = stage_bytes(BN, BK);
     static constexpr uint32_t bar_off = ST * SB;
-    // barrier area (8-byte aligned) after the stages
     static constexpr uint32_t full_off = bar_off;
     static constexpr uint32_t empty_off = full_off + 8 * ST;
     static constexpr uint32_t tfull_off = empty_off + 8 * ST;
@@ -139,8 +159,10 @@ struct Smem {
     static constexpr uint32_t abort_off = taddr_off + 4;
     static constexpr uint32_t flag_off = abort_off + 4;
     static constexpr uint32_t total = bar_off + kBarrierBytes + 1024;
+    static_assert(ST >= 2, "pipeline needs at least two stages");
     static_assert(flag_off + 4 <= bar_off + kBarrierBytes, "barrier area overflow");
     static_assert(total <= kSmemBudget, "shared memory overflow");
+    static_assert(A_BYTES % 1024 == 0 && SB % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b)
@@ -162,10 +184,22 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, int32_t (&acc)[W])
 }
 
 // Dequantises and stores W consecutive kernel columns [col0, col0+W) of
-// kernel row `row` (one thread = one row).
+// kernel row `row` (one thread = one row).  rsc is this row's scale;
+// csc_lane is the scale of column col0 + (lane % W), so the warp holds the
+// chunk's column scales in one register and shares them by shuffles.
+// Called by all 32 lanes of a warp (the shuffles precede any early exit).
 template <uint32_t W>
-__device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&acc)[W])
+__device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&acc)[W],
+                                            float rsc, float csc_lane)
 {
+    float v[W];
+    if (p.c_type != 2) {
+#pragma unroll
+        for (int j = 0; j < (int)W; ++j) {
+            const float csc = __shfl_sync(0xffffffffu, csc_lane, j);
+            v[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(rsc, csc));
+        }
+    }
     if (row >= p.Mk) return;
     if (p.c_type == 2) {  // raw int32
         int32_t* c = static_cast<int32_t*>(p.c);
@@ -186,14 +220,6 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
                 if (col0 + j < p.Nk) c[(size_t)(col0 + j) * p.ldc + row] = acc[j];
         }
         return;
-    }
-    const float rsc = p.row_scale_vec ? __ldg(p.row_scale_vec + row) : p.row_scale;
-    float v[W];
-#pragma unroll
-    for (int j = 0; j < (int)W; ++j) {
-        const uint32_t col = col0 + j;
-        const float csc = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + col) : 0.f) : p.col_scale;
-        v[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(rsc, csc));
     }
     uint16_t* c = static_cast<uint16_t*>(p.c);
     if (!p.transpose_out) {
@@ -231,16 +257,18 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
     }
 }
 
-template <uint32_t BN>
+template <uint32_t BN, uint32_t BK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p,
                    uint64_t wait_limit_ns)
 {
-    using L = Smem<BN>;
+    using L = Smem<BN, BK>;
     constexpr uint32_t ST = L::ST;
     constexpr uint32_t TMEM_COLS = tmem_cols(BN);
     constexpr uint32_t CW = BN < 32 ? BN : 32;  // columns per tcgen05.ld
     constexpr uint32_t NCH = BN / CW;
+    constexpr uint32_t KATOMS = BK / 128;       // 128-byte swizzle atoms along K per stage
+    constexpr uint32_t TILE_ELEMS = BN * kTileM;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -257,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
+        B2SQ_TRACE_POINT(0);
         for (uint32_t s = 0; s < ST; ++s) {
             mbar_init(full_bar + 8 * s, 1);
             mbar_init(empty_bar + 8 * s, 1);
@@ -278,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *taddr_slot;
+    if (threadIdx.x == 0) B2SQ_TRACE_POINT(1);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -303,16 +333,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t fb = full_bar + 8 * stage;
                     mbar_arrive_expect_tx(fb, L::SB);
                     const uint32_t sa = sbase + stage * L::SB;
-                    const uint32_t sb = sa + kABytes;
-                    const int32_t kc = (int32_t)(kb * kTileK);
-                    if (p.a_mn_major) tma_load_2d(sa, &tmA, fb, a_row, kc);
-                    else tma_load_2d(sa, &tmA, fb, kc, a_row);
-                    if (p.b_mn_major) {
+                    const uint32_t sb = sa + L::A_BYTES;
 #pragma unroll
-                        for (uint32_t j = 0; j < BN / 128; ++j)
-                            tma_load_2d(sb + j * (128 * kTileK), &tmB, fb, b_row + (int32_t)(j * 128), kc);
-                    } else {
-                        tma_load_2d(sb, &tmB, fb, kc, b_row);
+                    for (uint32_t i = 0; i < KATOMS; ++i) {
+                        const int32_t kc = (int32_t)(kb * BK + i * 128);
+                        // K-major: atom i is [128 rows][128 B]; MN-major: k rows are contiguous.
+                        if (p.a_mn_major) tma_load_2d(sa + i * (128 * 128), &tmA, fb, a_row, kc);
+                        else tma_load_2d(sa + i * (kTileM * 128), &tmA, fb, kc, a_row);
+                        if (p.b_mn_major) {
+#pragma unroll
+                            for (uint32_t j = 0; j < BN / 128; ++j)
+                                tma_load_2d(sb + j * (BK * 128) + i * (128 * 128), &tmB, fb, b_row + (int32_t)(j * 128),
+                                            kc);
+                        } else {
+                            tma_load_2d(sb + i * (BN * 128), &tmB, fb, kc, b_row);
+                        }
                     }
                     issued[stage] = true;
                     issued_phase[stage] = phase;
@@ -324,16 +359,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t s = 0; s < ST; ++s)
                 if (issued[s]) mbar_wait(full_bar + 8 * s, issued_phase[s], SITE_PRODUCER_DRAIN, nullptr, wait_limit_ns);
         }
+        __syncwarp();  // reconverge before the CTA-wide barrier below
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc_base = idesc_i8(kTileM, BN, 0, 0);
-            const uint32_t idesc = idesc_base | (p.a_mn_major << 15) | (p.b_mn_major << 16);
-            // Per-instruction (K = 32) descriptor advance inside a stage.
-            const uint32_t a_step = p.a_mn_major ? 32 * 128 : 32;
-            const uint32_t b_step = p.b_mn_major ? 32 * 128 : 32;
-            const uint32_t a_lbo = p.a_mn_major ? 128 * kTileK : 16;
-            const uint32_t b_lbo = p.b_mn_major ? 128 * kTileK : 16;
+            const uint32_t idesc = idesc_i8(kTileM, BN, p.a_mn_major, p.b_mn_major);
+            const uint32_t a_lbo = p.a_mn_major ? 128 * BK : 16;
+            const uint32_t b_lbo = p.b_mn_major ? 128 * BK : 16;
             UnitIter it;
             it.init(p);
             Unit u;
@@ -355,11 +387,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = sbase + stage * L::SB;
-                    const uint32_t sb = sa + kABytes;
+                    const uint32_t sb = sa + L::A_BYTES;
 #pragma unroll
-                    for (uint32_t kk = 0; kk < kTileK / 32; ++kk) {
-                        const uint64_t ad = umma_desc_sw128(sa + kk * a_step, a_lbo, 1024);
-                        const uint64_t bd = umma_desc_sw128(sb + kk * b_step, b_lbo, 1024);
+                    for (uint32_t kk = 0; kk < BK / 32; ++kk) {
+                        // K-major: atom kk/4, 32-byte step inside the swizzled row;
+                        // MN-major: 32 k rows of 128 bytes.
+                        const uint32_t a_off = p.a_mn_major ? kk * 32 * 128 : (kk / 4) * (kTileM * 128) + (kk % 4) * 32;
+                        const uint32_t b_off = p.b_mn_major ? kk * 32 * 128 : (kk / 4) * (BN * 128) + (kk % 4) * 32;
+                        const uint64_t ad = umma_desc_sw128(sa + a_off, a_lbo, 1024);
+                        const uint64_t bd = umma_desc_sw128(sb + b_off, b_lbo, 1024);
                         mma_i8(d_tmem, ad, bd, idesc, (kb > u.k0 || kk > 0) ? 1u : 0u);
                     }
                     mma_commit(empty_bar + 8 * stage);
@@ -370,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++uidx;
             }
         }
+        __syncwarp();  // reconverge before the CTA-wide barrier below
     } else {
         // ------------------------------------------------------------ epilogue
         const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
@@ -393,24 +430,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t row = tm * kTileM + row_local;
             const uint32_t taddr = tmem_base + ((q * 32) << 16) + buf * BN;
             const bool full = (u.k0 == 0 && u.k1 == p.k_blocks);
+            // Scales of this tile, fetched once: the row's own scale, and per
+            // lane the scale of column (chunk * CW + lane % CW) for every chunk.
+            const float rsc = (p.row_scale_vec && row < p.Mk) ? __ldg(p.row_scale_vec + row) : p.row_scale;
+            float csv[NCH];
+#pragma unroll
+            for (uint32_t ch = 0; ch < NCH; ++ch) {
+                const uint32_t col = tn * BN + ch * CW + (lane % CW);
+                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + col) : 0.f) : p.col_scale;
+            }
             if (full) {
-#pragma unroll 1
-                for (uint32_t ch = 0; ch < NCH; ++ch) {
+                if constexpr (NCH == 1) {
                     int32_t acc[CW];
-                    tmem_ld_chunk<CW>(taddr + ch * CW, acc);
+                    tmem_ld_chunk<CW>(taddr, acc);
                     tmem_ld_wait();
-                    if (ch == NCH - 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
+                    store_chunk<CW>(p, row, tn * BN, acc, rsc, csv[0]);
+                } else {
+                    // Two chunks per TMEM round trip.
+#pragma unroll
+                    for (uint32_t ch = 0; ch < NCH; ch += 2) {
+                        int32_t acc0[CW], acc1[CW];
+                        tmem_ld_chunk<CW>(taddr + ch * CW, acc0);
+                        tmem_ld_chunk<CW>(taddr + (ch + 1) * CW, acc1);
+                        tmem_ld_wait();
+                        if (ch + 2 >= NCH) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
+                        }
+                        store_chunk<CW>(p, row, tn * BN + ch * CW, acc0, rsc, csv[ch]);
+                        store_chunk<CW>(p, row, tn * BN + (ch + 1) * CW, acc1, rsc, csv[ch + 1]);
                     }
-                    store_chunk<CW>(p, row, tn * BN + ch * CW, acc);
                 }
             } else {
-                // Stream-K partial: accumulate into the workspace tile
-                // (column-major [BN][128] so a warp's adds are coalesced).
-                const uint32_t slot = u.tile - p.dp_tiles;
-                int32_t* wt = p.ws + (size_t)slot * (BN * kTileM);
+                if (ethread == 0) B2SQ_TRACE_POINT(2);
+                // Stream-K partial: store it to this CTA's slot ([BN][128],
+                // column-major so a warp's stores are 128-byte coalesced).
+                int32_t* my_slot = p.ws_slots + ((size_t)blockIdx.x * 2 + u.slot) * TILE_ELEMS;
 #pragma unroll 1
                 for (uint32_t ch = 0; ch < NCH; ++ch) {
                     int32_t acc[CW];
@@ -422,40 +481,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
                     }
 #pragma unroll
-                    for (uint32_t j = 0; j < CW; ++j) atomicAdd(wt + (size_t)(ch * CW + j) * kTileM + row_local, acc[j]);
+                    for (uint32_t j = 0; j < CW; ++j) __stcg(my_slot + (size_t)(ch * CW + j) * kTileM + row_local, acc[j]);
                 }
                 __threadfence();
                 named_bar_sync(1, kEpiThreads);
+                const uint32_t tail_idx = u.tile - p.dp_tiles;
                 if (ethread == 0) {
                     const uint32_t add = u.k1 - u.k0;
-                    const uint32_t old = atomicAdd(p.ws_cnt + slot, add);
-                    *epi_flag = (old + add == p.k_blocks) ? 1 : 0;
+                    const uint32_t old = atomicAdd(p.ws_cnt + tail_idx, add);
+                    const int last = (old + add == p.k_blocks) ? 1 : 0;
+                    if (last) p.ws_cnt[tail_idx] = 0;  // every contribution has arrived: reset for the next call
+                    *epi_flag = last;
                 }
                 named_bar_sync(1, kEpiThreads);
                 if (*epi_flag) {
-                    // This contribution completed the tile: finish it and
-                    // leave the workspace zeroed for the next call.
+                    // This contribution completed the tile: sum every
+                    // contributor's slot and run the epilogue.
                     __threadfence();
+                    const uint64_t it0 = (uint64_t)tail_idx * p.k_blocks;
+                    const uint64_t it1 = it0 + p.k_blocks;
+                    const uint64_t S = p.sk_iters, P = p.ctas;
+                    const uint32_t c_first = (uint32_t)(((it0 + 1) * P - 1) / S);
+                    const uint32_t c_last = (uint32_t)((it1 * P - 1) / S);
 #pragma unroll 1
                     for (uint32_t ch = 0; ch < NCH; ++ch) {
                         int32_t acc[CW];
 #pragma unroll
-                        for (uint32_t j = 0; j < CW; ++j) {
-                            int32_t* w = wt + (size_t)(ch * CW + j) * kTileM + row_local;
-                            acc[j] = __ldcg(w);
-                            __stcg(w, 0);
+                        for (uint32_t j = 0; j < CW; ++j) acc[j] = 0;
+#pragma unroll 1
+                        for (uint32_t cc = c_first; cc <= c_last; ++cc) {
+                            const uint64_t st = sk_start(cc, S, P);
+                            if (sk_start(cc + 1, S, P) == st) continue;  // CTA without stream-K work
+                            const uint32_t slot = st >= it0 ? 0u : 1u;
+                            const int32_t* src = p.ws_slots + ((size_t)cc * 2 + slot) * TILE_ELEMS;
+#pragma unroll
+                            for (uint32_t j = 0; j < CW; ++j) acc[j] += __ldcg(src + (size_t)(ch * CW + j) * kTileM + row_local);
                         }
-                        store_chunk<CW>(p, row, tn * BN + ch * CW, acc);
+                        store_chunk<CW>(p, row, tn * BN + ch * CW, acc, rsc, csv[ch]);
                     }
-                    if (ethread == 0) p.ws_cnt[slot] = 0;
                 }
             }
             ++uidx;
         }
     }
 
+    if (threadIdx.x == 64) B2SQ_TRACE_POINT(3);
+    if (threadIdx.x == 32) B2SQ_TRACE_POINT(4);
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) B2SQ_TRACE_POINT(5);
+    if (threadIdx.x == 64) B2SQ_TRACE_POINT(6);
+    if (threadIdx.x == 32) B2SQ_TRACE_POINT(7);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
@@ -484,7 +560,8 @@ EncodeTiledFn get_encode_fn()
     return fn;
 }
 
-// 2-D int8 operand map.  K-major: dims {K, rows}; MN-major: dims {rows, K}.
+// 2-D int8 operand map with a 128-byte swizzled box.  K-major: dims {K, rows},
+// box {128, box_rows}; MN-major: dims {rows, K}, box {128, 128}.
 bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint32_t K, uint32_t ld, bool mn_major,
                       uint32_t box_rows)
 {
@@ -496,11 +573,11 @@ bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint3
         dims[0] = rows;
         dims[1] = K;
         box[0] = 128;
-        box[1] = kTileK;
+        box[1] = 128;
     } else {
         dims[0] = K;
         dims[1] = rows;
-        box[0] = kTileK;
+        box[0] = 128;
         box[1] = box_rows;
     }
     cuuint64_t strides[1] = {ld};
@@ -511,10 +588,10 @@ bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint3
     return r == CUDA_SUCCESS;
 }
 
-template <uint32_t BN>
-cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
+template <uint32_t BN, uint32_t BK>
+cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
-    using L = Smem<BN>;
+    using L = Smem<BN, BK>;
     // The shared-memory opt-in is a per-device function attribute.
     static std::atomic<uint64_t> done_mask{0};
     int dev = 0;
@@ -522,11 +599,11 @@ cudaError_t launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const KParam
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_kernel<BN><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_kernel<BN, BK><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -540,29 +617,38 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_majo
     while (bn < Nk && bn < 256) bn <<= 1;
     if (b_mn_major && bn < 128) bn = 128;  // MN-major B tiles are 128-element swizzle rows
     s.tile_n = bn;
-    s.stages = num_stages(bn);
+    s.tile_k = tile_k_for(bn);
+    s.stages = num_stages(bn, s.tile_k);
     s.tiles_m = (Mk + kTileM - 1) / kTileM;
     s.tiles_n = (Nk + bn - 1) / bn;
-    s.k_blocks = (K + kTileK - 1) / kTileK;
+    s.k_blocks = (K + s.tile_k - 1) / s.tile_k;
     const uint64_t T = (uint64_t)s.tiles_m * s.tiles_n;
     const uint32_t P = num_sms ? num_sms : 148;
-    if (!allow_stream_k || s.k_blocks < 2 || (T % P == 0)) {
+    const uint64_t rounds = (T + P - 1) / P;
+    const double tail_loss = (double)(rounds * P - T) / (double)(rounds * P);
+    if (!allow_stream_k || s.k_blocks < 2 || tail_loss <= kStreamKMinTailLoss) {
         s.dp_tiles = (uint32_t)T;
         s.sk_iters = 0;
         s.ctas = (uint32_t)(T < P ? T : P);
     } else if (T >= 4ull * P) {
-        // Whole waves data-parallel, the partial last wave split by k-blocks.
+        // Whole rounds data-parallel, the partial last round split by k-blocks.
         s.dp_tiles = (uint32_t)((T / P) * P);
         s.sk_iters = (T - s.dp_tiles) * (uint64_t)s.k_blocks;
         s.ctas = P;
     } else {
-        // Few waves: stream-K over everything keeps every SM busy to the end.
+        // Few rounds: stream-K over everything keeps every SM busy to the end.
         s.dp_tiles = 0;
         s.sk_iters = T * (uint64_t)s.k_blocks;
         s.ctas = (uint32_t)(s.sk_iters < P ? s.sk_iters : P);
     }
     const uint64_t tail = T - s.dp_tiles;
-    s.workspace_bytes = tail ? (size_t)(tail * (uint64_t)bn * kTileM * 4 + ((tail * 4 + 255) & ~255ull)) : 0;
+    if (tail > kWsCounters) {  // more tail tiles than counters: whole tiles only
+        s.dp_tiles = (uint32_t)T;
+        s.sk_iters = 0;
+        s.ctas = (uint32_t)(T < P ? T : P);
+    } else if (tail) {
+        s.workspace_bytes = kWsCounterBytes + (size_t)s.ctas * 2 * bn * kTileM * 4;
+    }
 }
 
 cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* workspace, cudaStream_t st,
@@ -598,18 +684,17 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.row_scale = p.row_scale;
     kp.col_scale = p.col_scale;
     if (s.workspace_bytes) {
-        const uint64_t tail = (uint64_t)s.tiles_m * s.tiles_n - s.dp_tiles;
-        kp.ws = static_cast<int32_t*>(workspace);
-        kp.ws_cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + tail * bn * kTileM * 4);
+        kp.ws_cnt = static_cast<uint32_t*>(workspace);
+        kp.ws_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
     }
-    kp.raster_group = 16;
+    kp.raster_group = B2SQ_RASTER_GROUP;
     if (kp.ctas == 0) return cudaSuccess;
     switch (bn) {
-        case 16: return launch_bn<16>(ta, tb, kp, st);
-        case 32: return launch_bn<32>(ta, tb, kp, st);
-        case 64: return launch_bn<64>(ta, tb, kp, st);
-        case 128: return launch_bn<128>(ta, tb, kp, st);
-        case 256: return launch_bn<256>(ta, tb, kp, st);
+        case 16: return launch_tile<16, tile_k_for(16)>(ta, tb, kp, st);
+        case 32: return launch_tile<32, tile_k_for(32)>(ta, tb, kp, st);
+        case 64: return launch_tile<64, tile_k_for(64)>(ta, tb, kp, st);
+        case 128: return launch_tile<128, tile_k_for(128)>(ta, tb, kp, st);
+        case 256: return launch_tile<256, tile_k_for(256)>(ta, tb, kp, st);
         default:
             if (detail) *detail = "internal: unsupported tile_n";
             return cudaErrorInvalidValue;

@@ -35,6 +35,7 @@ struct GemmProblem {
 struct GemmSchedule {
     uint32_t swap_ab;
     uint32_t tile_n;
+    uint32_t tile_k;
     uint32_t stages;
     uint32_t tiles_m, tiles_n, k_blocks;
     uint32_t ctas;
@@ -43,8 +44,18 @@ struct GemmSchedule {
     size_t workspace_bytes;  // bytes of workspace the schedule needs (0 without stream-K)
 };
 
+// Stream-K is used only when whole-tile rounds would leave more than this
+// fraction of the last round's SM time idle.
+constexpr double kStreamKMinTailLoss = 0.05;
+
+// Stream-K workspace layout: a fixed header of per-tile k-block counters at
+// offset 0 (zero before the first call; every call leaves them zero), then
+// per-CTA partial-tile slots (scratch).  Keeping the counters at a fixed
+// place means calls of different shapes can share one workspace.
+constexpr uint32_t kWsCounters = 4096;
+constexpr size_t kWsCounterBytes = kWsCounters * sizeof(uint32_t);
+
 constexpr uint32_t kTileM = 128;
-constexpr uint32_t kTileK = 128;
 
 // Chooses tile_n, stages and the persistent/stream-K split (host only).
 void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_major, bool allow_stream_k,

@@ -52,6 +52,25 @@ __device__ __forceinline__ int8_t quant1(float xs, float inv, float qmax)
     return static_cast<int8_t>(fminf(fmaxf(rintf(v), -qmax), qmax));
 }
 
+// Fast form of quant1 for an integer qmax (<= 127), bit-identical to it for
+// every input including NaN and +-inf: clamp first (fmaxf maps NaN to -qmax,
+// as fmaxf(rintf(NaN), -qmax) does), then round to nearest even by adding
+// 1.5 * 2^23, which leaves rint(c) in the low mantissa bits in two's
+// complement.  Clamping before rounding equals rounding before clamping
+// because qmax is an integer.  Only FMA/ALU-pipe instructions, no
+// conversion-pipe (rint / float->int) work.
+__device__ __forceinline__ uint32_t quant_bits(float xs, float inv, float qmax)
+{
+    const float v = __fmul_rn(xs, inv);
+    const float c = fminf(fmaxf(v, -qmax), qmax);
+    return __float_as_uint(__fadd_rn(c, 12582912.0f));  // low byte = int8(rint(c))
+}
+
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3)
+{
+    return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
 __device__ __forceinline__ uint32_t pack4(int8_t a, int8_t b, int8_t c, int8_t d)
 {
     return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
@@ -109,15 +128,23 @@ __device__ __forceinline__ void quantize_store(const float (&xs)[VPT][8], float 
     const float rs = amax / qmax;  // IEEE division, reference :95
     if (row_ok && lane_in_group == 0) *rs_out = rs;
     const float inv = (rs > 0.f) ? (1.f / rs) : 0.f;  // reference :98
+    const bool integral_qmax = (qmax == truncf(qmax));
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const uint32_t v = j * G + lane_in_group;
         if (row_ok && v < nvec) {
             uint2 o;
-            o.x = pack4(quant1(xs[j][0], inv, qmax), quant1(xs[j][1], inv, qmax), quant1(xs[j][2], inv, qmax),
-                        quant1(xs[j][3], inv, qmax));
-            o.y = pack4(quant1(xs[j][4], inv, qmax), quant1(xs[j][5], inv, qmax), quant1(xs[j][6], inv, qmax),
-                        quant1(xs[j][7], inv, qmax));
+            if (integral_qmax) {
+                o.x = pack_low_bytes(quant_bits(xs[j][0], inv, qmax), quant_bits(xs[j][1], inv, qmax),
+                                     quant_bits(xs[j][2], inv, qmax), quant_bits(xs[j][3], inv, qmax));
+                o.y = pack_low_bytes(quant_bits(xs[j][4], inv, qmax), quant_bits(xs[j][5], inv, qmax),
+                                     quant_bits(xs[j][6], inv, qmax), quant_bits(xs[j][7], inv, qmax));
+            } else {
+                o.x = pack4(quant1(xs[j][0], inv, qmax), quant1(xs[j][1], inv, qmax), quant1(xs[j][2], inv, qmax),
+                            quant1(xs[j][3], inv, qmax));
+                o.y = pack4(quant1(xs[j][4], inv, qmax), quant1(xs[j][5], inv, qmax), quant1(xs[j][6], inv, qmax),
+                            quant1(xs[j][7], inv, qmax));
+            }
             *reinterpret_cast<uint2*>(yrow + (size_t)v * 8) = o;
         }
     }

@@ -121,6 +121,9 @@ def test_plan_choices():
     assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 0  # all stream-K
     p = api.plan(8192, 8192, 8192, num_sms=148)
     assert p.swap_ab == 0 and p.tile_n == 256 and p.tiles_m * p.tiles_n == 2048
-    assert p.dp_tiles == 13 * 148 and p.sk_iters == (2048 - 13 * 148) * 64
+    # 14 rounds of 148 with 124 tiles in the last: 1.2% idle, below the stream-K threshold
+    assert p.dp_tiles == 2048 and p.sk_iters == 0
+    p = api.plan(19 * 128, 20 * 256, 1024, num_sms=148)
+    assert p.dp_tiles == 0 and p.sk_iters == 380 * p.k_blocks  # 2.6 rounds: all stream-K
     p = api.plan(8192, 8192, 8192, api.ROW_MAJOR, api.ROW_MAJOR, num_sms=148)
     assert p.tile_n in (128, 256)

@@ -104,3 +104,24 @@ def test_bad_args_raise(cuda_device):
         api.smoothquant(x, s, quant_max=0.0)
     with pytest.raises(api.B2sqError):
         api.smoothquant(x, s, quant_max=200.0)
+
+
+@pytest.mark.parametrize("qmax", [127.0, 100.0, 7.0, 100.5, 126.9])
+def test_special_values_and_qmax(cuda_device, qmax):
+    """NaN / +-inf / subnormal / huge inputs and integral or fractional quant_max:
+    the fast rounding path (integral qmax) and the exact path must both match."""
+    rng = np.random.default_rng(int(qmax * 10))
+    M, N = 12, 2048
+    x = synth.activations_np(rng, M, N, 8, 20.0)
+    x[0, 3] = np.inf
+    x[1, 7] = -np.inf
+    x[2, 11] = np.nan
+    x[3, :] = np.float16(6e-8)       # subnormal fp16 everywhere
+    x[4, :] = 0
+    x[4, 100] = np.float16(65504)    # max fp16
+    x[5, 200] = np.nan
+    x[5, 201] = np.inf
+    s = synth.smooth_np(rng, N)
+    s[9] = 1e-30                     # tiny scale: subnormal products
+    check_sq(x, s, qmax)
+    check_sq(x[:, :1000].copy(), s[:1000].copy(), qmax)  # generic (unaligned-N) path too
