@@ -290,7 +290,10 @@ b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
 b2sq_status b2sq_last_device_error(b2sq_stream_t stream, uint32_t* where)
 {
     uint32_t v = 0;
+    uint32_t v_sq = 0;
     cudaError_t e = b2sq::read_and_clear_device_status(reinterpret_cast<cudaStream_t>(stream), &v);
+    if (e == cudaSuccess) e = b2sq::read_and_clear_sq_status(reinterpret_cast<cudaStream_t>(stream), &v_sq);
+    if (e == cudaSuccess && v == 0) v = v_sq;
     if (e != cudaSuccess) return cuda_fail(e, "last_device_error");
     if (where) *where = v;
     if (v != 0) return fail(B2SQ_ERR_TIMEOUT, "device wait gave up at site %u", v);

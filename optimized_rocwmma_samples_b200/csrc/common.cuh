@@ -29,6 +29,9 @@ enum WaitSite : uint32_t {
     SITE_MMA_TMEM_EMPTY = 3,
     SITE_EPI_TMEM_FULL = 4,
     SITE_PRODUCER_DRAIN = 5,
+    SITE_SQ_PRODUCER = 11,
+    SITE_SQ_CONSUMER = 12,
+    SITE_SQ_DRAIN = 13,
     SITE_DEBUG = 100,
 };
 

@@ -71,6 +71,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
 cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st);
 
 // Device status word access.
-cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value);
+cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value);  // gemm_i8.cu
+cudaError_t read_and_clear_sq_status(cudaStream_t st, uint32_t* value);      // smoothquant.cu
 
 }  // namespace b2sq

@@ -9,10 +9,11 @@
 // (IEEE division and round-to-nearest-even rint; the build has no fast-math.)
 //
 // Design (B200): the reference reads every row twice (pass 1 for the absmax,
-// pass 2 to quantise).  Here a group of G threads owns a row, loads it ONCE
-// with 128-bit non-allocating loads into registers, reduces the absmax with
-// warp shuffles (+ one shared-memory exchange when G > 32) and quantises from
-// registers with 64-bit int8 stores: one HBM read of x and one write of y.
+// pass 2 to quantise).  Here every row is read from HBM once: small inputs by
+// register-resident row groups (128-bit non-allocating loads, warp-shuffle
+// absmax), large inputs by a persistent kernel that stages whole rows in
+// shared memory with bulk TMA copies and writes whole int8 rows with bulk TMA
+// stores.
 // The MoE kernel reads each token row once for all of its top-k slots (the
 // reference re-reads it per slot).
 #include "common.cuh"
@@ -35,15 +36,53 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p)
     return v;
 }
 
+// fp16 pair -> two fp32, exactly.  Blackwell's mixed-precision add (fp16
+// operand, fp32 addend and result) of -0.0 runs on the FMA pipe; the plain
+// cvt.f32.f16 runs on the narrow conversion pipe, which would otherwise bound
+// this HBM kernel.  x + (-0.0) == x for every x (signed zeros included); NaN
+// payloads may differ, which no output observes.
+__device__ __forceinline__ void h2_to_f2(uint32_t w, float& lo, float& hi)
+{
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.f16 %0, l, %3;\n\tadd.rn.f32.f16 %1, h, %3;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(w), "f"(-0.0f));
+}
+
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8])
 {
-    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    h2_to_f2(v.x, f[0], f[1]);
+    h2_to_f2(v.y, f[2], f[3]);
+    h2_to_f2(v.z, f[4], f[5]);
+    h2_to_f2(v.w, f[6], f[7]);
+}
+
+// Packed pair multiply of sm_100 (mul.rn.f32x2): each lane is rounded exactly
+// like the scalar .rn multiply, at half the issue cost.  Used only where the
+// product feeds a max, never an add (an add could be contracted with it).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b)
+{
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b)
+{
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// xs[i] = x[i] * s[i] for one 8-wide vector, in pairs.
+__device__ __forceinline__ void scale8_pairs(const float (&xf)[8], const float (&sv)[8], float (&xs)[8])
+{
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float2 t = __half22float2(h[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
+    for (int i = 0; i < 8; i += 2)
+        f2_unpack(f2_mul(f2_pack(xf[i], xf[i + 1]), f2_pack(sv[i], sv[i + 1])), xs[i], xs[i + 1]);
 }
 
 __device__ __forceinline__ int8_t quant1(float xs, float inv, float qmax)
@@ -119,34 +158,56 @@ __device__ __forceinline__ void scale8(const float (&xf)[8], const float* s, flo
     xs[7] = __fmul_rn(xf[7], s1.w);
 }
 
+// Eight quantised values of one 16-byte input vector, packed into 8 bytes.
+__device__ __forceinline__ uint2 quantize8(const float (&xs)[8], float inv, float qmax, bool integral_qmax)
+{
+    uint2 o;
+    if (integral_qmax) {
+        o.x = pack_low_bytes(quant_bits(xs[0], inv, qmax), quant_bits(xs[1], inv, qmax), quant_bits(xs[2], inv, qmax),
+                             quant_bits(xs[3], inv, qmax));
+        o.y = pack_low_bytes(quant_bits(xs[4], inv, qmax), quant_bits(xs[5], inv, qmax), quant_bits(xs[6], inv, qmax),
+                             quant_bits(xs[7], inv, qmax));
+    } else {
+        o.x = pack4(quant1(xs[0], inv, qmax), quant1(xs[1], inv, qmax), quant1(xs[2], inv, qmax),
+                    quant1(xs[3], inv, qmax));
+        o.y = pack4(quant1(xs[4], inv, qmax), quant1(xs[5], inv, qmax), quant1(xs[6], inv, qmax),
+                    quant1(xs[7], inv, qmax));
+    }
+    return o;
+}
+
+// quantize8 for rows row_absmax() marked fast: |xs * inv| <= qmax(1 + 3 ulp),
+// so round-to-nearest-even by the 1.5 * 2^23 addition alone gives
+// clamp(rint(v)) exactly (qmax is an integer, so rint(v) never passes it).
+__device__ __forceinline__ uint2 quantize8_fast(const float (&xs)[8], float inv)
+{
+    // Scalar __fmul_rn / __fadd_rn: they are never contracted into an FMA,
+    // whose single rounding would differ from the reference's two on
+    // near-ties (packed f32x2 pairs are not safe here).
+    uint32_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = __float_as_uint(__fadd_rn(__fmul_rn(xs[i], inv), 12582912.0f));
+    return make_uint2(pack_low_bytes(b[0], b[1], b[2], b[3]), pack_low_bytes(b[4], b[5], b[6], b[7]));
+}
+
+// row_scale and its reciprocal, reference :95 and :98 (IEEE divisions).
+__device__ __forceinline__ float row_scale_of(float amax, float qmax) { return amax / qmax; }
+__device__ __forceinline__ float inv_scale_of(float rs) { return (rs > 0.f) ? (1.f / rs) : 0.f; }
+
 // Quantises one register-resident row slice and stores it.  Called by all
 // G threads of a row group.
 template <int G, int VPT>
 __device__ __forceinline__ void quantize_store(const float (&xs)[VPT][8], float amax, int8_t* yrow, float* rs_out,
                                                uint32_t nvec, float qmax, bool row_ok, int lane_in_group)
 {
-    const float rs = amax / qmax;  // IEEE division, reference :95
+    const float rs = row_scale_of(amax, qmax);
     if (row_ok && lane_in_group == 0) *rs_out = rs;
-    const float inv = (rs > 0.f) ? (1.f / rs) : 0.f;  // reference :98
+    const float inv = inv_scale_of(rs);
     const bool integral_qmax = (qmax == truncf(qmax));
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const uint32_t v = j * G + lane_in_group;
-        if (row_ok && v < nvec) {
-            uint2 o;
-            if (integral_qmax) {
-                o.x = pack_low_bytes(quant_bits(xs[j][0], inv, qmax), quant_bits(xs[j][1], inv, qmax),
-                                     quant_bits(xs[j][2], inv, qmax), quant_bits(xs[j][3], inv, qmax));
-                o.y = pack_low_bytes(quant_bits(xs[j][4], inv, qmax), quant_bits(xs[j][5], inv, qmax),
-                                     quant_bits(xs[j][6], inv, qmax), quant_bits(xs[j][7], inv, qmax));
-            } else {
-                o.x = pack4(quant1(xs[j][0], inv, qmax), quant1(xs[j][1], inv, qmax), quant1(xs[j][2], inv, qmax),
-                            quant1(xs[j][3], inv, qmax));
-                o.y = pack4(quant1(xs[j][4], inv, qmax), quant1(xs[j][5], inv, qmax), quant1(xs[j][6], inv, qmax),
-                            quant1(xs[j][7], inv, qmax));
-            }
-            *reinterpret_cast<uint2*>(yrow + (size_t)v * 8) = o;
-        }
+        if (row_ok && v < nvec) *reinterpret_cast<uint2*>(yrow + (size_t)v * 8) = quantize8(xs[j], inv, qmax, integral_qmax);
     }
 }
 
@@ -244,6 +305,311 @@ __global__ void __launch_bounds__(kThreads) moe_sq_vec_kernel(const __half* __re
         amax = group_max<G>(amax, red[k & 1]);
         quantize_store<G, VPT>(xs, amax, qy + (size_t)r * hidden, row_scale + r, nvec, qmax, ok, lane_in_group);
     }
+}
+
+// ---------------------------------------------------------------------------
+// Streaming variant for large inputs: persistent CTAs; whole fp16 rows are
+// staged into a ring of shared-memory buffers by 1-D bulk TMA copies
+// (cp.async.bulk) that a producer warp keeps several rows ahead, so HBM
+// always has rows in flight while eight consumer warps reduce and quantise.
+// Each consumer thread owns the same columns of every row, so its smooth
+// scales live in registers.  Quantised rows are assembled in one of two
+// shared-memory rows and written by a single bulk store (whole-row writes).
+// ---------------------------------------------------------------------------
+constexpr int kTmaConsumers = 256;  // 8 warps
+constexpr int kTmaThreads = kTmaConsumers + 32;
+constexpr int kTmaMaxStages = 8;
+constexpr uint32_t kTmaReserved = 512;  // barriers, reduction slots, abort flag
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most one bulk store group still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's shared-memory writes before later async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void sts64(uint32_t addr, uint2 v)
+{
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(v.x), "r"(v.y) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+struct TmaRing {
+    uint32_t data;   // smem address of stage 0
+    uint32_t full;   // kTmaMaxStages barriers
+    uint32_t empty;  // kTmaMaxStages barriers
+    float* red;      // [2 parities][2 reductions][8 warps] per-warp maxima
+    volatile int* abort;
+};
+
+__device__ __forceinline__ TmaRing tma_ring(uint8_t* smem, uint32_t stages, uint32_t stage_bytes)
+{
+    TmaRing r;
+    r.data = smem_u32(smem);
+    const uint32_t bars = r.data + stages * stage_bytes;
+    r.full = bars;
+    r.empty = bars + 8 * kTmaMaxStages;
+    r.red = reinterpret_cast<float*>(smem + stages * stage_bytes + 16 * kTmaMaxStages);
+    r.abort = reinterpret_cast<volatile int*>(smem + stages * stage_bytes + 16 * kTmaMaxStages + 128);
+    return r;
+}
+
+__device__ __forceinline__ void tma_ring_init(const TmaRing& r, uint32_t stages)
+{
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(r.full + 8 * s, 1);
+            mbar_init(r.empty + 8 * s, kTmaConsumers / 32);
+        }
+        *r.abort = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+}
+
+// Producer loop: row i of this CTA is global row blockIdx.x + i * gridDim.x.
+__device__ __forceinline__ void tma_produce(const TmaRing& r, const __half* x, uint64_t rows, uint32_t row_elems,
+                                            uint32_t stages, uint32_t stage_bytes)
+{
+    const uint32_t bytes = row_elems * 2;
+    uint32_t i = 0;
+    for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x, ++i) {
+        const uint32_t s = i % stages, ph = (i / stages) & 1;
+        if (!mbar_wait(r.empty + 8 * s, ph ^ 1, SITE_SQ_PRODUCER, r.abort)) return;
+        mbar_arrive_expect_tx(r.full + 8 * s, bytes);
+        bulk_load(r.data + s * stage_bytes, x + row * row_elems, bytes, r.full + 8 * s);
+    }
+    // Drain the copies still in flight before the CTA may exit.
+    for (uint32_t k = i > stages ? i - stages : 0; k < i; ++k)
+        mbar_wait(r.full + 8 * (k % stages), (k / stages) & 1, SITE_SQ_DRAIN, nullptr);
+}
+
+// Consumer side: wait for row i, copy this thread's vectors to registers and
+// release the stage.  Returns false if the wait gave up.
+template <int VPT>
+__device__ __forceinline__ bool tma_consume(const TmaRing& r, uint32_t i, uint32_t stages, uint32_t stage_bytes,
+                                            uint32_t nvec, uint4 (&raw)[VPT])
+{
+    const uint32_t s = i % stages, ph = (i / stages) & 1;
+    if (!mbar_wait(r.full + 8 * s, ph, SITE_SQ_CONSUMER, r.abort)) return false;
+    const uint32_t base = r.data + s * stage_bytes;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const uint32_t v = j * kTmaConsumers + threadIdx.x;
+        raw[j] = v < nvec ? lds128(base + v * 16) : make_uint4(0, 0, 0, 0);
+    }
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(r.empty + 8 * s);
+    return true;
+}
+
+// max that returns NaN if either operand is NaN (fmaxf ignores NaN).
+__device__ __forceinline__ float max_nan(float a, float b)
+{
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// Block-wide max over the 8 consumer warps.  slot selects one of four 8-float
+// areas, (row parity, reduction), so each reduction of a row needs a single
+// barrier.  kNanProp chooses max.NaN (propagating) or fmaxf (ignoring).
+template <bool kNanProp>
+__device__ __forceinline__ float consumers_max(float v, float* red, uint32_t slot)
+{
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, v, off);
+        v = kNanProp ? max_nan(v, o) : fmaxf(v, o);
+    }
+    if ((threadIdx.x & 31) == 0) red[slot * 8 + (threadIdx.x >> 5)] = v;
+    named_bar_sync(1, kTmaConsumers);
+    float m = red[slot * 8];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = kNanProp ? max_nan(m, red[slot * 8 + w]) : fmaxf(m, red[slot * 8 + w]);
+    return m;
+}
+
+// Row absmax with the reference's NaN-ignoring fmaxf (:83-84), computed the
+// cheap way: a NaN-propagating max first; only a row holding a NaN pays a
+// second, NaN-ignoring reduction.  *fast tells the caller that the row is
+// free of NaN and +-inf products and its reciprocal scale is finite, so every
+// x*s*inv lies within qmax*(1 + 3 ulp) and needs no clamping.
+template <int VPT>
+__device__ __forceinline__ float row_absmax(const float (&xs)[VPT][8], float* red, uint32_t parity, float qmax,
+                                            bool* fast)
+{
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a = max_nan(a, fabsf(xs[j][k]));
+    float amax = consumers_max<true>(a, red, parity * 2);
+    const bool has_nan = amax != amax;
+    if (has_nan) {  // block-uniform
+        a = 0.f;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) a = fmaxf(a, fabsf(xs[j][k]));
+        amax = consumers_max<false>(a, red, parity * 2 + 1);
+    }
+    const float inv = inv_scale_of(row_scale_of(amax, qmax));
+    *fast = !has_nan && isfinite(amax) && isfinite(inv) && qmax == truncf(qmax);
+    return amax;
+}
+
+// Quantises a row held by the 256 consumer threads and writes it out.  With
+// out_bytes != 0 (row length a multiple of 16 bytes, y 16-byte aligned) the
+// int8 row is assembled in one of two shared-memory rows and written by one
+// bulk store; otherwise each thread stores its 8-byte pieces.
+template <int VPT>
+__device__ __forceinline__ void tma_quantize_out(const float (&xs)[VPT][8], float amax, bool fast, int8_t* yrow,
+                                                 float* rs_out, uint32_t nvec, float qmax, bool ok, uint32_t out_buf,
+                                                 uint32_t out_bytes)
+{
+    if (out_bytes == 0) {
+        quantize_store<kTmaConsumers, VPT>(xs, amax, yrow, rs_out, nvec, qmax, ok, threadIdx.x);
+        return;
+    }
+    const float rs = row_scale_of(amax, qmax);
+    const float inv = inv_scale_of(rs);
+    const bool integral_qmax = (qmax == truncf(qmax));
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const uint32_t v = j * kTmaConsumers + threadIdx.x;
+        if (v < nvec) sts64(out_buf + v * 8, fast ? quantize8_fast(xs[j], inv) : quantize8(xs[j], inv, qmax, integral_qmax));
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(2, kTmaConsumers);
+    if (threadIdx.x == 0) {
+        if (ok) {
+            *rs_out = rs;
+            bulk_store(yrow, out_buf, out_bytes);
+        }
+        // The other buffer is rewritten for the next row only after this
+        // thread reaches that row's first barrier, i.e. after this wait.
+        bulk_wait_read_1();
+    }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kTmaThreads) sq_tma_kernel(const __half* __restrict__ x,
+                                                             const float* __restrict__ smooth,
+                                                             int8_t* __restrict__ y, float* __restrict__ row_scale,
+                                                             uint32_t M, uint32_t N, float qmax, uint32_t stages,
+                                                             uint32_t stage_bytes, uint32_t out_bytes)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const TmaRing r = tma_ring(smem, stages, stage_bytes);
+    const uint32_t out_base = r.data + stages * stage_bytes + kTmaReserved;
+    const uint32_t out_stride = (out_bytes + 127) & ~127u;
+    tma_ring_init(r, stages);
+    const uint32_t nvec = N / 8;
+    if (threadIdx.x >= kTmaConsumers) {
+        if (threadIdx.x == kTmaConsumers) tma_produce(r, x, M, N, stages, stage_bytes);
+        return;
+    }
+    float sv[VPT][8];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+        const uint32_t v = j * kTmaConsumers + threadIdx.x;
+        if (v < nvec) {
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(smooth + (size_t)v * 8));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(smooth + (size_t)v * 8) + 1);
+            sv[j][0] = s0.x, sv[j][1] = s0.y, sv[j][2] = s0.z, sv[j][3] = s0.w;
+            sv[j][4] = s1.x, sv[j][5] = s1.y, sv[j][6] = s1.z, sv[j][7] = s1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sv[j][i] = 0.f;
+        }
+    }
+    uint32_t i = 0;
+    for (uint64_t row = blockIdx.x; row < M; row += gridDim.x, ++i) {
+        uint4 raw[VPT];
+        if (!tma_consume<VPT>(r, i, stages, stage_bytes, nvec, raw)) break;
+        float xs[VPT][8];
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+            float xf[8];
+            unpack8(raw[j], xf);
+            scale8_pairs(xf, sv[j], xs[j]);
+        }
+        bool fast;
+        const float amax = row_absmax<VPT>(xs, r.red, i & 1, qmax, &fast);
+        tma_quantize_out<VPT>(xs, amax, fast, y + row * N, row_scale + row, nvec, qmax, true,
+                              out_base + (i & 1) * out_stride, out_bytes);
+    }
+    if (threadIdx.x == 0) bulk_wait_all();
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kTmaThreads) moe_sq_tma_kernel(const __half* __restrict__ x,
+                                                                 const float* __restrict__ smooth,
+                                                                 const int32_t* __restrict__ topk_ids,
+                                                                 int8_t* __restrict__ qy,
+                                                                 float* __restrict__ row_scale, uint32_t tokens,
+                                                                 uint32_t hidden, uint32_t topk, uint32_t experts,
+                                                                 float qmax, const int32_t* __restrict__ row_perm,
+                                                                 uint32_t stages, uint32_t stage_bytes, uint32_t out_bytes)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const TmaRing r = tma_ring(smem, stages, stage_bytes);
+    const uint32_t out_base = r.data + stages * stage_bytes + kTmaReserved;
+    const uint32_t out_stride = (out_bytes + 127) & ~127u;
+    tma_ring_init(r, stages);
+    const uint32_t nvec = hidden / 8;
+    if (threadIdx.x >= kTmaConsumers) {
+        if (threadIdx.x == kTmaConsumers) tma_produce(r, x, tokens, hidden, stages, stage_bytes);
+        return;
+    }
+    uint32_t i = 0, parity = 0;
+    for (uint64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x, ++i) {
+        uint4 raw[VPT];
+        if (!tma_consume<VPT>(r, i, stages, stage_bytes, nvec, raw)) break;
+#pragma unroll 1
+        for (uint32_t k = 0; k < topk; ++k, parity ^= 1) {
+            const uint64_t flat = tok * topk + k;
+            const int32_t eid = __ldg(topk_ids + flat);
+            const int64_t rr = row_perm ? (int64_t)__ldg(row_perm + flat) : (int64_t)flat;
+            const bool ok = eid >= 0 && (uint32_t)eid < experts && rr >= 0;  // reference :86-87
+            const float* srow = smooth + (size_t)(ok ? eid : 0) * hidden;
+            float xs[VPT][8];
+#pragma unroll
+            for (int j = 0; j < VPT; ++j) {
+                const uint32_t v = j * kTmaConsumers + threadIdx.x;
+                float xf[8];
+                unpack8(raw[j], xf);
+                if (ok && v < nvec) {
+                    scale8(xf, srow + (size_t)v * 8, xs[j]);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) xs[j][q] = 0.f;
+                }
+            }
+            bool fast;
+            const float amax = row_absmax<VPT>(xs, r.red, parity, qmax, &fast);
+            tma_quantize_out<VPT>(xs, amax, fast, qy + (size_t)rr * hidden, row_scale + rr, nvec, qmax, ok,
+                                  out_base + parity * out_stride, out_bytes);
+        }
+    }
+    if (threadIdx.x == 0) bulk_wait_all();
 }
 
 // Generic fallback: one block per output row, two passes over the row (the
@@ -375,6 +741,107 @@ unsigned generic_grid(uint64_t rows)
 
 }  // namespace
 
+// ------------------------------------------------------------- streaming path
+namespace {
+
+// Inputs of at least this many elements take the streaming kernels.
+constexpr uint64_t kTmaMinElems = 1ull << 22;
+constexpr uint32_t kTmaRingBytes = 110 * 1024;  // input ring per CTA: two CTAs per SM for 16 KiB rows
+
+struct TmaCfg {
+    uint32_t stages, stage_bytes, out_bytes, smem;
+};
+
+// Input ring of whole fp16 rows, plus two int8 output rows when the output
+// can be written by bulk stores (row bytes a multiple of 16, y 16-B aligned).
+TmaCfg tma_cfg(uint32_t row_elems, const void* y)
+{
+    TmaCfg c;
+    c.stage_bytes = (row_elems * 2 + 127) & ~127u;
+    const uint32_t s = kTmaRingBytes / c.stage_bytes;
+    c.stages = s < 2 ? 2 : (s > (uint32_t)kTmaMaxStages ? (uint32_t)kTmaMaxStages : s);
+    c.out_bytes = (row_elems % 16 == 0 && aligned(y, 16)) ? row_elems : 0;
+    c.smem = c.stages * c.stage_bytes + kTmaReserved + 2 * ((c.out_bytes + 127) & ~127u);
+    return c;
+}
+
+// Grid of a persistent kernel: SM count x resident CTAs per SM, capped by the work.
+template <typename Kern>
+cudaError_t persistent_grid(Kern kern, uint32_t smem, uint64_t work, unsigned* grid)
+{
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTmaThreads, smem);
+    if (e != cudaSuccess) return e;
+    const uint64_t cap = (uint64_t)sms * (per_sm > 0 ? per_sm : 1);
+    *grid = (unsigned)(work < cap ? work : cap);
+    return cudaSuccess;
+}
+
+template <int VPT>
+cudaError_t launch_sq_tma(const __half* x, const float* s, int8_t* y, float* rs, uint32_t M, uint32_t N, float qmax,
+                          cudaStream_t st)
+{
+    const TmaCfg c = tma_cfg(N, y);
+    unsigned grid = 0;
+    cudaError_t e = persistent_grid(sq_tma_kernel<VPT>, c.smem, M, &grid);
+    if (e != cudaSuccess) return e;
+    sq_tma_kernel<VPT><<<grid, kTmaThreads, c.smem, st>>>(x, s, y, rs, M, N, qmax, c.stages, c.stage_bytes,
+                                                          c.out_bytes);
+    return cudaGetLastError();
+}
+
+template <int VPT>
+cudaError_t launch_moe_tma(const __half* x, const float* s, const int32_t* ids, int8_t* qy, float* rs, uint32_t T,
+                           uint32_t H, uint32_t K, uint32_t E, float qmax, const int32_t* perm, cudaStream_t st)
+{
+    const TmaCfg c = tma_cfg(H, qy);
+    unsigned grid = 0;
+    cudaError_t e = persistent_grid(moe_sq_tma_kernel<VPT>, c.smem, T, &grid);
+    if (e != cudaSuccess) return e;
+    moe_sq_tma_kernel<VPT><<<grid, kTmaThreads, c.smem, st>>>(x, s, ids, qy, rs, T, H, K, E, qmax, perm, c.stages,
+                                                              c.stage_bytes, c.out_bytes);
+    return cudaGetLastError();
+}
+
+#define B2SQ_TMA_DISPATCH(FN, VPT, ...)        \
+    switch (VPT) {                             \
+        case 1: return FN<1>(__VA_ARGS__);     \
+        case 2: return FN<2>(__VA_ARGS__);     \
+        case 3: return FN<3>(__VA_ARGS__);     \
+        case 4: return FN<4>(__VA_ARGS__);     \
+        case 5: return FN<5>(__VA_ARGS__);     \
+        case 6: return FN<6>(__VA_ARGS__);     \
+        case 7: return FN<7>(__VA_ARGS__);     \
+        case 8: return FN<8>(__VA_ARGS__);     \
+        default: return cudaErrorInvalidValue; \
+    }
+
+bool use_tma(uint64_t rows, uint32_t row_elems, uint32_t& vpt)
+{
+    const uint32_t nvec = row_elems / 8;
+    vpt = (nvec + kTmaConsumers - 1) / kTmaConsumers;
+    return rows * row_elems >= kTmaMinElems && vpt >= 1 && vpt <= 8 && row_elems * 2 <= kTmaRingBytes / 2;
+}
+
+}  // namespace
+
+cudaError_t read_and_clear_sq_status(cudaStream_t st, uint32_t* value)
+{
+    uint32_t v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && v != 0) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    *value = v;
+    return e;
+}
+
 cudaError_t launch_smoothquant(const void* x, const float* s, int8_t* y, float* rs, uint32_t M, uint32_t N, float qmax,
                                cudaStream_t st, int* used_vector_path)
 {
@@ -385,6 +852,11 @@ cudaError_t launch_smoothquant(const void* x, const float* s, int8_t* y, float* 
     if (!vec_ok) {
         sq_generic_kernel<<<generic_grid(M), kThreads, 0, st>>>(xh, s, y, rs, M, N, qmax);
         return cudaGetLastError();
+    }
+    uint32_t vpt = 0;
+    if (use_tma(M, N, vpt)) {
+        if (used_vector_path) *used_vector_path = 2;
+        B2SQ_TMA_DISPATCH(launch_sq_tma, vpt, xh, s, y, rs, M, N, qmax, st)
     }
     B2SQ_VEC_DISPATCH(launch_sq, xh, s, y, rs, M, N, qmax, st)
 }
@@ -401,6 +873,11 @@ cudaError_t launch_moe_smoothquant(const void* x, const float* s, const int32_t*
         moe_sq_generic_kernel<<<generic_grid((uint64_t)T * K), kThreads, 0, st>>>(xh, s, ids, qy, rs, T, H, K, E,
                                                                                   qmax, perm);
         return cudaGetLastError();
+    }
+    uint32_t vpt = 0;
+    if (use_tma(T, H, vpt)) {
+        if (used_vector_path) *used_vector_path = 2;
+        B2SQ_TMA_DISPATCH(launch_moe_tma, vpt, xh, s, ids, qy, rs, T, H, K, E, qmax, perm, st)
     }
     B2SQ_VEC_DISPATCH(launch_moe, xh, s, ids, qy, rs, T, H, K, E, qmax, perm, st)
 }

@@ -69,3 +69,17 @@ def test_moe_c5_shape(cuda_device):
     ids = synth.topk_routing_np(rng, synth.MOE_TOKENS, synth.MOE_EXPERTS, synth.MOE_TOPK)
     q, r, q0, r0 = run_moe(x, s, ids, sentinel=False)
     assert np.array_equal(q, q0) and np.array_equal(r, r0)
+
+
+def test_moe_streaming_special_values(cuda_device):
+    rng = np.random.default_rng(78)
+    T, H, E, K = 1024, 4096, 8, 2
+    x = synth.activations_np(rng, T, H, 8, 20.0)
+    x[3, 5] = np.nan
+    x[4, 6] = np.inf
+    x[5, :] = 0
+    s = synth.smooth_np(rng, H, E)
+    ids = synth.topk_routing_np(rng, T, E, K)
+    ids[7, 1] = 99
+    q, r, q0, r0 = run_moe(x, s, ids)
+    assert np.array_equal(q, q0) and np.array_equal(r.view(np.uint32), r0.view(np.uint32))
