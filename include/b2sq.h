@@ -134,6 +134,30 @@ B2SQ_API b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k,
                          void* workspace, size_t workspace_bytes,
                          b2sq_stream_t stream);
 
+/*
+ * b2sq_gemm_i8 without a caller-provided workspace (no counterpart in the
+ * reference): for callers that cannot allocate device memory, e.g. a host
+ * bound over a plain C FFI with no device allocator, or a serving process
+ * that has given all of HBM to its own pool and must not call cudaMalloc on
+ * the request path.  The stream-K scratch comes from a fixed 16 MiB array
+ * compiled into the library, resident on every GPU that loads it until the
+ * process exits; nothing is allocated.  Shapes whose schedule needs more
+ * scratch than that return B2SQ_ERR_UNSUPPORTED (use b2sq_gemm_i8 with a
+ * workspace); all skinny-M (M <= 64) decode shapes and every shape without
+ * stream-K fit.  Arguments and results are those of b2sq_gemm_i8.
+ * The first call on a device looks up the array's device address (once per
+ * device); make that first call before any stream capture.  Every call
+ * shares the array and clears its counters itself: calls that overlap on the
+ * GPU (other streams or unordered host threads) race on it.
+ */
+B2SQ_API b2sq_status b2sq_gemm_i8_no_alloc(uint32_t m, uint32_t n, uint32_t k,
+                                           const int8_t* a, b2sq_layout la, uint32_t lda,
+                                           const int8_t* b, b2sq_layout lb, uint32_t ldb,
+                                           void* c, b2sq_dtype c_type, uint32_t ldc,
+                                           const float* scale_a_row, const float* scale_b_col,
+                                           float scale_a, float scale_b,
+                                           b2sq_stream_t stream);
+
 /* Bytes of workspace that let b2sq_gemm_i8 use stream-K for this shape
  * (0 when the chosen schedule never splits a tile).  Host only. */
 B2SQ_API b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k,

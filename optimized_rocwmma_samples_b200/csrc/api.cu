@@ -124,6 +124,8 @@ b2sq_status validate_gemm(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b
 
 }  // namespace
 
+b2sq_status b2sq::set_last_error(b2sq_status s, const char* msg) { return fail(s, "%s", msg); }
+
 extern "C" {
 
 const char* b2sq_version(void) { return "b2sq 0.1.0 (sm_100a)"; }

@@ -6,6 +6,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "../../include/b2sq.h"
+
 namespace b2sq {
 
 cudaError_t launch_smoothquant(const void* x, const float* s, int8_t* y, float* rs, uint32_t M, uint32_t N,
@@ -73,5 +75,9 @@ cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st);
 // Device status word access.
 cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value);  // gemm_i8.cu
 cudaError_t read_and_clear_sq_status(cudaStream_t st, uint32_t* value);      // smoothquant.cu
+
+// Sets the calling thread's message returned by b2sq_last_error_message()
+// and returns s (defined in api.cu).
+b2sq_status set_last_error(b2sq_status s, const char* msg);
 
 }  // namespace b2sq
