@@ -180,6 +180,8 @@ typedef struct {
     uint32_t dp_tiles;       /* tiles computed whole, in data-parallel order */
     uint32_t sk_iters_per_cta_floor; /* stream-K k-blocks per CTA (floor) */
     uint64_t sk_iters;       /* total stream-K k-blocks over the tail tiles */
+    uint32_t cta_pair;       /* 1: tiles are computed by CTA pairs (two SMs, 256-row tiles);
+                                ctas counts CTAs, i.e. twice the number of pairs */
 } b2sq_gemm_plan;
 
 B2SQ_API b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k,

@@ -39,6 +39,7 @@ class GemmPlan(C.Structure):
         ("dp_tiles", C.c_uint32),
         ("sk_iters_per_cta_floor", C.c_uint32),
         ("sk_iters", C.c_uint64),
+        ("cta_pair", C.c_uint32),
     ]
 
 

@@ -191,10 +191,11 @@ b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k, b2sq_layout la
     }
     const Mapped mp = map_operands(m, n, la, lb);
     b2sq::GemmSchedule s;
-    b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.b_mn, use_stream_k != 0, num_sms, s);
+    b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.a_mn, mp.b_mn, use_stream_k != 0, num_sms, s);
     std::memset(plan, 0, sizeof(*plan));
     plan->swap_ab = mp.swap;
-    plan->tile_m = b2sq::kTileM;
+    plan->tile_m = s.cta_pair ? 2 * b2sq::kTileM : b2sq::kTileM;
+    plan->cta_pair = s.cta_pair;
     plan->tile_n = s.tile_n;
     plan->tile_k = s.tile_k;
     plan->stages = s.stages;
@@ -221,7 +222,7 @@ b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k, b2sq
     if (e != cudaSuccess) return cuda_fail(e, "gemm_i8_workspace_size: SM count");
     const Mapped mp = map_operands(m, n, la, lb);
     b2sq::GemmSchedule s;
-    b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.b_mn, true, sms, s);
+    b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.a_mn, mp.b_mn, true, sms, s);
     *bytes = s.workspace_bytes;
     return ok();
 }
@@ -275,9 +276,9 @@ b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
         p.col_scale = scale_b;
     }
     b2sq::GemmSchedule s;
-    b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.b_mn_major, workspace != nullptr, sms, s);
+    b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.a_mn_major, p.b_mn_major, workspace != nullptr, sms, s);
     if (s.workspace_bytes > 0 && (workspace == nullptr || workspace_bytes < s.workspace_bytes))
-        b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.b_mn_major, false, sms, s);
+        b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.a_mn_major, p.b_mn_major, false, sms, s);
     if (s.workspace_bytes > 0 && !aligned(workspace, 256))
         return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8: workspace must be 256-byte aligned");
     const char* detail = nullptr;

@@ -538,6 +538,184 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair kernel for large K-major problems: a cluster of two CTAs (two SMs)
+// computes a 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256, N = 256).
+// Each CTA loads its own 128 rows of A and its own 128 rows (columns of the
+// product) of B per stage, so every SM streams half of the B panel a 1-CTA
+// 128 x 256 tile would need; each CTA's TMEM holds its 128 x 256 half of the
+// accumulator.  Only the leader (rank 0) issues MMAs; both CTAs' TMA copies
+// signal the leader's "full" barrier; the leader's commits release "empty"
+// stages and "accumulator full" in both CTAs; both CTAs' epilogue warps
+// release an accumulator on the leader's "accumulator empty" barrier.
+// Whole tiles only (data-parallel rounds), used when the last round leaves at
+// most 5% of the pairs idle.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kPairBN = 256;  // tile columns (MMA N)
+constexpr uint32_t kPairBK = 128;
+constexpr uint32_t kPairHalfBytes = 128 * kPairBK;          // 16 KiB: one operand half per stage
+constexpr uint32_t kPairSB = 2 * kPairHalfBytes;            // A half + B half per CTA per stage
+constexpr uint32_t kPairST = 6;
+constexpr uint32_t kPairBarOff = kPairST * kPairSB;
+constexpr uint32_t kPairSmem = kPairBarOff + kBarrierBytes + 1024;
+static_assert(kPairSmem <= kSmemBudget, "pair kernel shared memory overflow");
+
+__global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const KParams p, uint64_t wait_limit_ns)
+{
+    constexpr uint32_t ST = kPairST;
+    constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t full_bar = sbase + kPairBarOff;
+    const uint32_t empty_bar = full_bar + 8 * ST;
+    const uint32_t tfull_bar = empty_bar + 8 * ST;
+    const uint32_t tempty_bar = tfull_bar + 16;
+    volatile uint32_t* taddr_slot = reinterpret_cast<volatile uint32_t*>(smem + kPairBarOff + 16 * ST + 32);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairBarOff + 16 * ST + 36);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t pair = blockIdx.x >> 1;
+    const uint32_t npairs = gridDim.x >> 1;
+    const uint32_t T = p.tiles_m * p.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < ST; ++s) {
+            mbar_init(full_bar + 8 * s, 1);
+            mbar_init(empty_bar + 8 * s, 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar + 8 * b, 1);
+            mbar_init(tempty_bar + 8 * b, 8);  // four epilogue warps in each CTA of the pair
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(const_cast<uint32_t*>(taddr_slot)), TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers initialised before any remote use
+    tc_fence_after();
+    const uint32_t tmem_base = *taddr_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (uint32_t t = pair; ok && t < T; t += npairs) {
+                uint32_t tm, tn;
+                tile_coords(p, t, tm, tn);
+                const int32_t a_row = (int32_t)(tm * 256 + rank * 128);
+                const int32_t b_row = (int32_t)(tn * kPairBN + rank * 128);
+                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_bar + 8 * stage;
+                    if (rank == 0) mbar_arrive_expect_tx(fb, 2 * kPairSB);  // both CTAs' bytes
+                    const uint32_t fb_leader = mapa_shared(fb, 0);
+                    const uint32_t sa = sbase + stage * kPairSB;
+                    const int32_t kc = (int32_t)(kb * kPairBK);
+                    tma_load_2d_pair(sa, &tmA, fb_leader, kc, a_row);
+                    tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, kc, b_row);
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader only)
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = idesc_i8(256, kPairBN, 0, 0);
+            uint32_t stage = 0, phase = 0, uidx = 0;
+            bool ok = true;
+            for (uint32_t t = pair; ok && t < T; t += npairs, ++uidx) {
+                const uint32_t buf = uidx & 1, use = uidx >> 1;
+                if (!mbar_wait(tempty_bar + 8 * buf, (use & 1) ^ 1, SITE_MMA_TMEM_EMPTY, abort_flag, wait_limit_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * kPairBN;
+                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = sbase + stage * kPairSB;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kPairBK / 32; ++kk) {
+                        const uint64_t ad = umma_desc_sw128(sa + kk * 32, 16, 1024);
+                        const uint64_t bd = umma_desc_sw128(sa + kPairHalfBytes + kk * 32, 16, 1024);
+                        mma_i8_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit_pair(empty_bar + 8 * stage, 0x3);
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_bar + 8 * buf, 0x3);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const uint32_t q = warp & 3;
+        const uint32_t row_local = q * 32 + lane;
+        constexpr uint32_t CW = 32, NCH = kPairBN / CW;
+        uint32_t uidx = 0;
+        for (uint32_t t = pair; t < T; t += npairs, ++uidx) {
+            const uint32_t buf = uidx & 1, use = uidx >> 1;
+            if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) break;
+            tc_fence_after();
+            uint32_t tm, tn;
+            tile_coords(p, t, tm, tn);
+            const uint32_t row = tm * 256 + rank * 128 + row_local;
+            const uint32_t taddr = tmem_base + ((q * 32) << 16) + buf * kPairBN;
+            const float rsc = (p.row_scale_vec && row < p.Mk) ? __ldg(p.row_scale_vec + row) : p.row_scale;
+            float csv[NCH];
+#pragma unroll
+            for (uint32_t ch = 0; ch < NCH; ++ch) {
+                const uint32_t col = tn * kPairBN + ch * CW + lane;
+                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + col) : 0.f) : p.col_scale;
+            }
+#pragma unroll
+            for (uint32_t ch = 0; ch < NCH; ch += 2) {
+                int32_t acc0[CW], acc1[CW];
+                tmem_ld_chunk<CW>(taddr + ch * CW, acc0);
+                tmem_ld_chunk<CW>(taddr + (ch + 1) * CW, acc1);
+                tmem_ld_wait();
+                if (ch + 2 >= NCH) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
+                }
+                store_chunk<CW>(p, row, tn * kPairBN + ch * CW, acc0, rsc, csv[ch]);
+                store_chunk<CW>(p, row, tn * kPairBN + (ch + 1) * CW, acc1, rsc, csv[ch + 1]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
 // --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
@@ -607,12 +785,50 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     return cudaGetLastError();
 }
 
+cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
+{
+    static std::atomic<uint64_t> done_mask{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done_mask.load() & bit)) {
+        e = cudaFuncSetAttribute(gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+        if (e != cudaSuccess) return e;
+        done_mask.fetch_or(bit);
+    }
+    gemm_i8_pair_kernel<<<kp.ctas, kThreads, kPairSmem, st>>>(ta, tb, kp, kWaitLimitNs);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
-void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_major, bool allow_stream_k,
-                        uint32_t num_sms, GemmSchedule& s)
+void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_major, uint32_t b_mn_major,
+                        bool allow_stream_k, uint32_t num_sms, GemmSchedule& s)
 {
     s = GemmSchedule{};
+    const uint32_t P = num_sms ? num_sms : 148;
+#ifndef B2SQ_DISABLE_PAIR
+    // CTA-pair 256 x 256 tiles for large K-major problems whose whole-tile
+    // rounds leave at most kStreamKMinTailLoss of the pairs idle.
+    if (!a_mn_major && !b_mn_major && Mk >= 256 && Nk >= 256 && P >= 2) {
+        const uint64_t tm2 = (Mk + 255) / 256, tn2 = (Nk + kPairBN - 1) / kPairBN, T2 = tm2 * tn2;
+        const uint64_t pairs = P / 2, rounds = (T2 + pairs - 1) / pairs;
+        const double loss = (double)(rounds * pairs - T2) / (double)(rounds * pairs);
+        if (T2 >= pairs && loss <= kStreamKMinTailLoss) {
+            s.cta_pair = 1;
+            s.tile_n = kPairBN;
+            s.tile_k = kPairBK;
+            s.stages = kPairST;
+            s.tiles_m = (uint32_t)tm2;
+            s.tiles_n = (uint32_t)tn2;
+            s.k_blocks = (K + kPairBK - 1) / kPairBK;
+            s.dp_tiles = (uint32_t)T2;
+            s.ctas = (uint32_t)(2 * pairs);
+            return;
+        }
+    }
+#endif
     uint32_t bn = 16;
     while (bn < Nk && bn < 256) bn <<= 1;
     if (b_mn_major && bn < 128) bn = 128;  // MN-major B tiles are 128-element swizzle rows
@@ -623,7 +839,6 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_majo
     s.tiles_n = (Nk + bn - 1) / bn;
     s.k_blocks = (K + s.tile_k - 1) / s.tile_k;
     const uint64_t T = (uint64_t)s.tiles_m * s.tiles_n;
-    const uint32_t P = num_sms ? num_sms : 148;
     const uint64_t rounds = (T + P - 1) / P;
     const double tail_loss = (double)(rounds * P - T) / (double)(rounds * P);
     if (!allow_stream_k || s.k_blocks < 2 || tail_loss <= kStreamKMinTailLoss) {
@@ -657,7 +872,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     const uint32_t bn = s.tile_n;
     CUtensorMap ta, tb;
     if (!make_operand_map(&ta, p.a, p.Mk, p.K, p.lda, p.a_mn_major != 0, kTileM) ||
-        !make_operand_map(&tb, p.b, p.Nk, p.K, p.ldb, p.b_mn_major != 0, bn)) {
+        !make_operand_map(&tb, p.b, p.Nk, p.K, p.ldb, p.b_mn_major != 0, s.cta_pair ? 128 : bn)) {
         if (detail) *detail = "cuTensorMapEncodeTiled rejected an operand (alignment / stride)";
         return cudaErrorInvalidValue;
     }
@@ -689,6 +904,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     }
     kp.raster_group = B2SQ_RASTER_GROUP;
     if (kp.ctas == 0) return cudaSuccess;
+    if (s.cta_pair) return launch_pair(ta, tb, kp, st);
     switch (bn) {
         case 16: return launch_tile<16, tile_k_for(16)>(ta, tb, kp, st);
         case 32: return launch_tile<32, tile_k_for(32)>(ta, tb, kp, st);

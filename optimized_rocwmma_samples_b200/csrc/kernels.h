@@ -38,6 +38,7 @@ struct GemmSchedule {
     uint32_t swap_ab;
     uint32_t tile_n;
     uint32_t tile_k;
+    uint32_t cta_pair;  // 1: CTA-pair kernel, 256-row tiles
     uint32_t stages;
     uint32_t tiles_m, tiles_n, k_blocks;
     uint32_t ctas;
@@ -60,8 +61,8 @@ constexpr size_t kWsCounterBytes = kWsCounters * sizeof(uint32_t);
 constexpr uint32_t kTileM = 128;
 
 // Chooses tile_n, stages and the persistent/stream-K split (host only).
-void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t b_mn_major, bool allow_stream_k,
-                        uint32_t num_sms, GemmSchedule& s);
+void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_major, uint32_t b_mn_major,
+                        bool allow_stream_k, uint32_t num_sms, GemmSchedule& s);
 
 // Launches the tcgen05 GEMM.  workspace may be null only if
 // s.workspace_bytes == 0.  Returns a CUDA error or cudaSuccess; *detail gets

@@ -83,11 +83,12 @@ def simulate_units(pl):
     T = pl.tiles_m * pl.tiles_n
     kb = pl.k_blocks
     cover = {}
-    for cta in range(pl.ctas):
+    workers = pl.ctas // 2 if pl.cta_pair else pl.ctas  # a CTA pair shares one work list
+    for cta in range(workers):
         t = cta
         while t < pl.dp_tiles:
             cover.setdefault(t, []).append((0, kb))
-            t += pl.ctas
+            t += workers
         pos = cta * pl.sk_iters // pl.ctas
         end = (cta + 1) * pl.sk_iters // pl.ctas
         while pos < end:
@@ -120,9 +121,11 @@ def test_plan_choices():
     p = api.plan(16, 28672, 8192, num_sms=148)
     assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 0  # all stream-K
     p = api.plan(8192, 8192, 8192, num_sms=148)
-    assert p.swap_ab == 0 and p.tile_n == 256 and p.tiles_m * p.tiles_n == 2048
-    # 14 rounds of 148 with 124 tiles in the last: 1.2% idle, below the stream-K threshold
-    assert p.dp_tiles == 2048 and p.sk_iters == 0
+    # CTA pairs: 1024 tiles of 256 x 256 over 74 pairs, 14 rounds, 1.2% idle
+    assert p.cta_pair == 1 and p.swap_ab == 0 and p.tile_m == 256 and p.tile_n == 256
+    assert p.tiles_m * p.tiles_n == 1024 and p.dp_tiles == 1024 and p.sk_iters == 0 and p.ctas == 148
+    p = api.plan(8192, 8192, 8192, api.COL_MAJOR, api.COL_MAJOR, num_sms=148)  # MN-major A: one CTA per tile
+    assert p.cta_pair == 0 and p.tile_n == 256 and p.dp_tiles == 2048 and p.sk_iters == 0
     p = api.plan(19 * 128, 20 * 256, 1024, num_sms=148)
     assert p.dp_tiles == 0 and p.sk_iters == 380 * p.k_blocks  # 2.6 rounds: all stream-K
     p = api.plan(8192, 8192, 8192, api.ROW_MAJOR, api.ROW_MAJOR, num_sms=148)
