@@ -190,6 +190,55 @@ B2SQ_API b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k,
                               b2sq_gemm_plan* plan);
 
 /* ------------------------------------------------------------------------ */
+/* MoE: grouping by expert and the grouped (per-expert) GEMM                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Replaces the histogram / padded prefix / scatter kernels of
+ * rocwmma_moe_sorting.cpp (:53-77, :82-101, :107-125).  For topk_ids
+ * [tokens, topk]:
+ *   expert_count[e]     valid (token, slot) pairs routed to expert e
+ *   expert_start[e]     start of e's segment, segments padded to unit_size;
+ *                       expert_start[experts] = padded total
+ *   sorted_token_ids    token id of each pair in its expert's segment
+ *                       (capacity tokens*topk + experts*unit_size); padding
+ *                       slots hold the sentinel `tokens`
+ *   row_perm (nullable) sorted position of every flat index t*topk+k, -1 for
+ *                       an expert id outside [0, experts)
+ * The order inside a segment is stable (increasing flat index): one of the
+ * orders the reference's atomic scatter can produce, but reproducible.
+ * experts <= 1024, unit_size >= 1.
+ */
+B2SQ_API b2sq_status b2sq_moe_sorting(const int32_t* topk_ids, uint32_t tokens, uint32_t topk,
+                                      uint32_t experts, uint32_t unit_size,
+                                      int32_t* expert_count, int32_t* expert_start,
+                                      int32_t* sorted_token_ids, int32_t* row_perm,
+                                      b2sq_stream_t stream);
+
+/*
+ * Grouped int8 GEMM over expert segments (the grouped GEMM of
+ * rocwmma_grouped_gemm.cpp:104-122, with the per-group descriptors replaced
+ * by the sorting outputs, which stay on the device).  For every group g:
+ *   rows r in [group_start[g], group_start[g] + group_count[g]):
+ *   c[r, n] = cvt_rn(float(sum_k a[r,k] * w[g][n][k]) * (sa * sb))
+ * with sa = scale_a_row ? scale_a_row[r] : scale_a and
+ *      sb = scale_b_col ? scale_b_col[g*n_cols + n] : scale_b.
+ * a: int8 [rows, k] row-major (lda >= k, lda % 16 == 0): the activations in
+ *    expert-sorted order (b2sq_moe_smoothquant with row_perm writes them so);
+ * w: int8 [groups][n][k] K-major weights, row pitch ldb (>= k, % 16 == 0);
+ * c: row-major [rows, n] (ldc >= n); rows outside every segment are not
+ * written.  groups <= 1024; rows = capacity of a / c in rows.
+ */
+B2SQ_API b2sq_status b2sq_gemm_i8_grouped(uint32_t groups, uint32_t rows, uint32_t n, uint32_t k,
+                                          const int8_t* a, uint32_t lda,
+                                          const int8_t* w, uint32_t ldb,
+                                          void* c, b2sq_dtype c_type, uint32_t ldc,
+                                          const float* scale_a_row, const float* scale_b_col,
+                                          float scale_a, float scale_b,
+                                          const int32_t* group_start, const int32_t* group_count,
+                                          b2sq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Diagnostics                                                              */
 /* ------------------------------------------------------------------------ */
 

@@ -14,7 +14,9 @@ from .api import (  # noqa: F401
     kernel_moe_smoothquant,
     kernel_smoothquant,
     last_device_error,
+    gemm_grouped,
     moe_smoothquant,
+    moe_sorting,
     plan,
     smoothquant,
     workspace_size,

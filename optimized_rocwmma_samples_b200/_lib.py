@@ -63,6 +63,9 @@ SIGNATURES = {
                                    _vp, _vp, _f32, _f32, _vp]),
     "b2sq_gemm_i8_workspace_size": (_i, [_u32, _u32, _u32, _i, _i, C.POINTER(_sz)]),
     "b2sq_gemm_i8_plan": (_i, [_u32, _u32, _u32, _i, _i, _i, _u32, C.POINTER(GemmPlan)]),
+    "b2sq_moe_sorting": (_i, [_vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "b2sq_gemm_i8_grouped": (_i, [_u32, _u32, _u32, _u32, _vp, _u32, _vp, _u32, _vp, _i, _u32, _vp, _vp,
+                                  _f32, _f32, _vp, _vp, _vp]),
     "b2sq_status_string": (C.c_char_p, [_i]),
     "b2sq_last_error_message": (C.c_char_p, []),
     "b2sq_last_device_error": (_i, [_vp, C.POINTER(_u32)]),

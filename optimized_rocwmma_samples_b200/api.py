@@ -221,3 +221,51 @@ def debug_bounded_wait(timeout_us: int, stream: Optional[torch.cuda.Stream] = No
 kernel_smoothquant = smoothquant
 kernel_moe_smoothquant = moe_smoothquant
 gemm_quant_tensor_scale = gemm_quant
+
+
+# ----------------------------------------------------------------------------- MoE
+def moe_sorting(topk_ids: torch.Tensor, experts: int, unit_size: int = 1,
+                stream: Optional[torch.cuda.Stream] = None):
+    """Groups (token, slot) pairs by expert (rocwmma_moe_sorting.cpp).
+
+    Returns (expert_count [E], expert_start [E+1], sorted_token_ids
+    [tokens*topk + E*unit_size], row_perm [tokens*topk]), all int32 on the device.
+    """
+    if topk_ids.dtype != torch.int32 or topk_ids.dim() != 2 or not topk_ids.is_contiguous():
+        raise ValueError("topk_ids must be a contiguous int32 [tokens, topk] tensor")
+    T, K = topk_ids.shape
+    dev = _need_cuda(topk_ids)
+    count = torch.empty((experts,), dtype=torch.int32, device=dev)
+    start = torch.empty((experts + 1,), dtype=torch.int32, device=dev)
+    sorted_ids = torch.empty((T * K + experts * unit_size,), dtype=torch.int32, device=dev)
+    row_perm = torch.empty((T * K,), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    st = lib.b2sq_moe_sorting(topk_ids.data_ptr(), T, K, experts, unit_size, count.data_ptr(), start.data_ptr(),
+                              sorted_ids.data_ptr(), row_perm.data_ptr(), _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_moe_sorting")
+    return count, start, sorted_ids, row_perm
+
+
+def gemm_grouped(a: torch.Tensor, w: torch.Tensor, group_start: torch.Tensor, group_count: torch.Tensor,
+                 scale_a_row: Optional[torch.Tensor] = None, scale_b_col: Optional[torch.Tensor] = None,
+                 scale_a: float = 1.0, scale_b: float = 1.0, out_dtype: torch.dtype = torch.bfloat16,
+                 c: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Per-expert GEMM over expert-sorted rows: a int8 [rows, K] row-major,
+    w int8 [E, N, K] (K-major weights), group_start/group_count int32 [>=E].
+    Rows outside every group are left untouched in c."""
+    if a.dtype != torch.int8 or w.dtype != torch.int8 or a.dim() != 2 or w.dim() != 3:
+        raise ValueError("a must be int8 [rows, K], w int8 [E, N, K]")
+    rows, K = a.shape
+    E, N, K2 = w.shape
+    if K2 != K or a.stride(1) != 1 or w.stride(2) != 1 or w.stride(0) != w.stride(1) * N:
+        raise ValueError("shape/layout mismatch between a and w")
+    if c is None:
+        c = torch.zeros((rows, N), dtype=out_dtype, device=a.device)
+    dev = _need_cuda(a, w, c, group_start, group_count, scale_a_row, scale_b_col)
+    lib = _lib.load()
+    st = lib.b2sq_gemm_i8_grouped(E, rows, N, K, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(1),
+                                  c.data_ptr(), _DTYPE_CODE[out_dtype], c.stride(0), _ptr(scale_a_row),
+                                  _ptr(scale_b_col), float(scale_a), float(scale_b), group_start.data_ptr(),
+                                  group_count.data_ptr(), _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_gemm_i8_grouped")
+    return c

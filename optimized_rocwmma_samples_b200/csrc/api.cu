@@ -290,6 +290,69 @@ b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
     return ok();
 }
 
+b2sq_status b2sq_moe_sorting(const int32_t* topk_ids, uint32_t tokens, uint32_t topk, uint32_t experts,
+                             uint32_t unit_size, int32_t* expert_count, int32_t* expert_start,
+                             int32_t* sorted_token_ids, int32_t* row_perm, b2sq_stream_t stream)
+{
+    if (experts == 0 || experts > 1024) return fail(B2SQ_ERR_INVALID_ARG, "moe_sorting: experts must be in [1, 1024]");
+    if (unit_size == 0) return fail(B2SQ_ERR_INVALID_ARG, "moe_sorting: unit_size must be >= 1");
+    if ((uint64_t)tokens * topk > 0x7fffffffull) return fail(B2SQ_ERR_INVALID_ARG, "moe_sorting: too many rows");
+    if (!expert_count || !expert_start || ((uint64_t)tokens * topk > 0 && (!topk_ids || !sorted_token_ids)))
+        return fail(B2SQ_ERR_INVALID_ARG, "moe_sorting: null pointer");
+    cudaError_t e = b2sq::launch_moe_sort(topk_ids, tokens, topk, experts, unit_size, expert_count, expert_start,
+                                          sorted_token_ids, row_perm, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "moe_sorting launch");
+    return ok();
+}
+
+b2sq_status b2sq_gemm_i8_grouped(uint32_t groups, uint32_t rows, uint32_t n, uint32_t k, const int8_t* a,
+                                 uint32_t lda, const int8_t* w, uint32_t ldb, void* c, b2sq_dtype c_type,
+                                 uint32_t ldc, const float* scale_a_row, const float* scale_b_col, float scale_a,
+                                 float scale_b, const int32_t* group_start, const int32_t* group_count,
+                                 b2sq_stream_t stream)
+{
+    if (c_type != B2SQ_F16 && c_type != B2SQ_BF16 && c_type != B2SQ_I32)
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: bad output dtype %d", (int)c_type);
+    if (groups == 0 || rows == 0 || n == 0) return ok();
+    if (groups > b2sq::kMaxGroups) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: groups must be <= 1024");
+    if (k == 0) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: k must be >= 1");
+    if (!a || !w || !c || !group_start || !group_count)
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: null pointer");
+    if (lda < k || ldb < k || ldc < n) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: leading dimension too small");
+    if ((uint64_t)groups * n > 0xffffffffull) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: groups*n too large");
+    if (!aligned(c, c_type == B2SQ_I32 ? 4 : 2)) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_grouped: c misaligned");
+    if (!aligned(a, 16) || !aligned(w, 16) || lda % 16 || ldb % 16)
+        return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8_grouped: a, w 16-byte aligned and lda, ldb multiples of 16 (TMA)");
+    uint32_t sms = 0;
+    cudaError_t e = current_sm_count(&sms);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_i8_grouped: SM count");
+    b2sq::GroupedProblem g{};
+    g.groups = groups;
+    g.rows = rows;
+    g.N = n;
+    g.K = k;
+    g.a = a;
+    g.lda = lda;
+    g.b = w;
+    g.ldb = ldb;
+    g.c = c;
+    g.ldc = ldc;
+    g.c_type = (int)c_type;
+    g.row_scale_vec = scale_a_row;
+    g.col_scale_vec = scale_b_col;
+    g.row_scale = scale_a;
+    g.col_scale = scale_b;
+    g.group_start = group_start;
+    g.group_count = group_count;
+    const char* detail = nullptr;
+    e = b2sq::launch_gemm_i8_grouped(g, sms, reinterpret_cast<cudaStream_t>(stream), &detail);
+    if (e != cudaSuccess) {
+        if (detail) return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8_grouped: %s", detail);
+        return cuda_fail(e, "gemm_i8_grouped launch");
+    }
+    return ok();
+}
+
 b2sq_status b2sq_last_device_error(b2sq_stream_t stream, uint32_t* where)
 {
     uint32_t v = 0;

@@ -91,6 +91,24 @@ struct KParams {
     uint32_t* ws_cnt;   // [tail tiles] k-blocks accumulated so far (zero between calls)
     int32_t* ws_slots;  // [ctas][2][tile_n][128] int32 partial tiles (scratch)
     uint32_t raster_group;
+    // Grouped (MoE) mode: group g owns rows [grp_start[g], grp_start[g] + grp_count[g])
+    // of A and C, rows [g * Nk, (g + 1) * Nk) of B and entries [g * Nk, ...) of
+    // the column scales.
+    const int32_t* grp_start;
+    const int32_t* grp_count;
+    uint32_t groups;
+};
+
+constexpr uint32_t kTileK_Grouped = tile_k_for(256);
+
+// Where one tile reads and writes.
+struct TileGeom {
+    uint32_t a_row;    // first A row (TMA coordinate)
+    uint32_t b_row;    // first B row
+    uint32_t c_row;    // first C row of the tile
+    uint32_t row_end;  // C rows at or beyond this are not written
+    uint32_t col0;     // first C column
+    uint32_t cs_off;   // offset of this tile's group in the column scales
 };
 
 struct Unit {
@@ -106,15 +124,19 @@ struct UnitIter {
     uint32_t dp_next;
     uint64_t sk_pos, sk_begin, sk_end;
 
-    __device__ __forceinline__ void init(const KParams& p)
+    uint32_t dp_total;
+
+    __device__ __forceinline__ void init(const KParams& p) { init(p, p.dp_tiles); }
+    __device__ __forceinline__ void init(const KParams& p, uint32_t dp_tiles)
     {
+        dp_total = dp_tiles;
         dp_next = blockIdx.x;
         sk_begin = sk_pos = sk_start(blockIdx.x, p.sk_iters, p.ctas);
         sk_end = sk_start(blockIdx.x + 1, p.sk_iters, p.ctas);
     }
     __device__ __forceinline__ bool next(const KParams& p, Unit& u)
     {
-        if (dp_next < p.dp_tiles) {
+        if (dp_next < dp_total) {
             u = {dp_next, 0, p.k_blocks, 0};
             dp_next += p.ctas;
             return true;
@@ -143,6 +165,45 @@ __device__ __forceinline__ void tile_coords(const KParams& p, uint32_t t, uint32
     const uint32_t r = t - g * per_group;
     tm = first_m + r % gsize;
     tn = r / gsize;
+}
+
+// Tile geometry.  Plain mode: raster-grouped (tm, tn).  Grouped mode: the
+// group is found by binary search of the per-group tile prefix `gpre`
+// (the scheme of rocwmma_grouped_gemm.cpp:111-122); inside a group the M
+// tiles run fastest so a group's B panel is reused while it is in L2.
+template <bool kGrouped, uint32_t BN>
+__device__ __forceinline__ TileGeom tile_geom(const KParams& p, uint32_t t, const uint32_t* gpre)
+{
+    TileGeom g;
+    if constexpr (kGrouped) {
+        uint32_t lo = 0, hi = p.groups;  // gpre[lo] <= t < gpre[hi]
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (gpre[mid] <= t) lo = mid;
+            else hi = mid;
+        }
+        const uint32_t tl = t - gpre[lo];
+        const uint32_t cnt = (uint32_t)p.grp_count[lo];
+        const uint32_t tme = (cnt + kTileM - 1) / kTileM;
+        const uint32_t tm = tl % tme, tn = tl / tme;
+        const uint32_t start = (uint32_t)p.grp_start[lo];
+        g.a_row = start + tm * kTileM;
+        g.c_row = g.a_row;
+        g.row_end = start + cnt;
+        g.b_row = lo * p.Nk + tn * BN;
+        g.col0 = tn * BN;
+        g.cs_off = lo * p.Nk;
+    } else {
+        uint32_t tm, tn;
+        tile_coords(p, t, tm, tn);
+        g.a_row = tm * kTileM;
+        g.c_row = g.a_row;
+        g.row_end = p.Mk;
+        g.b_row = tn * BN;
+        g.col0 = tn * BN;
+        g.cs_off = 0;
+    }
+    return g;
 }
 
 template <uint32_t BN, uint32_t BK>
@@ -257,7 +318,7 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
     }
 }
 
-template <uint32_t BN, uint32_t BK>
+template <uint32_t BN, uint32_t BK, bool kGrouped>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p,
                    uint64_t wait_limit_ns)
@@ -306,6 +367,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    uint32_t* gpre = nullptr;  // grouped mode: tile prefix per group, [groups + 1]
+    uint32_t tiles_total = p.dp_tiles;
+    if constexpr (kGrouped) {
+        __shared__ uint32_t s_gpre[kMaxGroups + 1];
+        gpre = s_gpre;
+        if (threadIdx.x == 0) {
+            uint32_t acc = 0;
+            for (uint32_t g = 0; g < p.groups; ++g) {
+                s_gpre[g] = acc;
+                const uint32_t cnt = p.grp_count[g] > 0 ? (uint32_t)p.grp_count[g] : 0u;
+                acc += ((cnt + kTileM - 1) / kTileM) * p.tiles_n;
+            }
+            s_gpre[p.groups] = acc;
+        }
+        __syncthreads();
+        tiles_total = s_gpre[p.groups];
+    }
     const uint32_t tmem_base = *taddr_slot;
     if (threadIdx.x == 0) B2SQ_TRACE_POINT(1);
 
@@ -313,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             UnitIter it;
-            it.init(p);
+            it.init(p, tiles_total);
             Unit u;
             uint32_t stage = 0, phase = 0;
             uint32_t issued_phase[8];
@@ -321,10 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t s = 0; s < 8; ++s) issued[s] = false, issued_phase[s] = 0;
             bool ok = true;
             while (ok && it.next(p, u)) {
-                uint32_t tm, tn;
-                tile_coords(p, u.tile, tm, tn);
-                const int32_t a_row = (int32_t)(tm * kTileM);
-                const int32_t b_row = (int32_t)(tn * BN);
+                const TileGeom tg = tile_geom<kGrouped, BN>(p, u.tile, gpre);
+                const int32_t a_row = (int32_t)tg.a_row;
+                const int32_t b_row = (int32_t)tg.b_row;
                 for (uint32_t kb = u.k0; kb < u.k1; ++kb) {
                     if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
                         ok = false;
@@ -367,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t a_lbo = p.a_mn_major ? 128 * BK : 16;
             const uint32_t b_lbo = p.b_mn_major ? 128 * BK : 16;
             UnitIter it;
-            it.init(p);
+            it.init(p, tiles_total);
             Unit u;
             uint32_t stage = 0, phase = 0, uidx = 0;
             bool ok = true;
@@ -413,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t row_local = q * 32 + lane;
         const uint32_t ethread = threadIdx.x - 64;
         UnitIter it;
-        it.init(p);
+        it.init(p, tiles_total);
         Unit u;
         uint32_t uidx = 0;
         bool ok = true;
@@ -425,9 +502,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            uint32_t tm, tn;
-            tile_coords(p, u.tile, tm, tn);
-            const uint32_t row = tm * kTileM + row_local;
+            const TileGeom tg = tile_geom<kGrouped, BN>(p, u.tile, gpre);
+            const uint32_t tn_col0 = tg.col0;
+            // Rows past the tile's limit (the matrix, or the group in grouped
+            // mode) get an out-of-range index so store_chunk skips them.
+            const uint32_t row = tg.c_row + row_local < tg.row_end ? tg.c_row + row_local : 0xffffffffu;
             const uint32_t taddr = tmem_base + ((q * 32) << 16) + buf * BN;
             const bool full = (u.k0 == 0 && u.k1 == p.k_blocks);
             // Scales of this tile, fetched once: the row's own scale, and per
@@ -436,8 +515,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             float csv[NCH];
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ++ch) {
-                const uint32_t col = tn * BN + ch * CW + (lane % CW);
-                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + col) : 0.f) : p.col_scale;
+                const uint32_t col = tn_col0 + ch * CW + (lane % CW);
+                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f)
+                                          : p.col_scale;
             }
             if (full) {
                 if constexpr (NCH == 1) {
@@ -447,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
-                    store_chunk<CW>(p, row, tn * BN, acc, rsc, csv[0]);
+                    store_chunk<CW>(p, row, tn_col0, acc, rsc, csv[0]);
                 } else {
                     // Two chunks per TMEM round trip.
 #pragma unroll
@@ -461,8 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __syncwarp();
                             if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
                         }
-                        store_chunk<CW>(p, row, tn * BN + ch * CW, acc0, rsc, csv[ch]);
-                        store_chunk<CW>(p, row, tn * BN + (ch + 1) * CW, acc1, rsc, csv[ch + 1]);
+                        store_chunk<CW>(p, row, tn_col0 + ch * CW, acc0, rsc, csv[ch]);
+                        store_chunk<CW>(p, row, tn_col0 + (ch + 1) * CW, acc1, rsc, csv[ch + 1]);
                     }
                 }
             } else {
@@ -517,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (uint32_t j = 0; j < CW; ++j) acc[j] += __ldcg(src + (size_t)(ch * CW + j) * kTileM + row_local);
                         }
-                        store_chunk<CW>(p, row, tn * BN + ch * CW, acc, rsc, csv[ch]);
+                        store_chunk<CW>(p, row, tn_col0 + ch * CW, acc, rsc, csv[ch]);
                     }
                 }
             }
@@ -766,7 +846,7 @@ bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint3
     return r == CUDA_SUCCESS;
 }
 
-template <uint32_t BN, uint32_t BK>
+template <uint32_t BN, uint32_t BK, bool kGrouped = false>
 cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
     using L = Smem<BN, BK>;
@@ -777,11 +857,12 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 L::total);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_kernel<BN, BK><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_kernel<BN, BK, kGrouped><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -915,6 +996,41 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
             if (detail) *detail = "internal: unsupported tile_n";
             return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_gemm_i8_grouped(const GroupedProblem& g, uint32_t num_sms, cudaStream_t st, const char** detail)
+{
+    constexpr uint32_t BN = 256;
+    CUtensorMap ta, tb;
+    if (!make_operand_map(&ta, g.a, g.rows, g.K, g.lda, false, kTileM) ||
+        !make_operand_map(&tb, g.b, g.groups * g.N, g.K, g.ldb, false, BN)) {
+        if (detail) *detail = "cuTensorMapEncodeTiled rejected an operand (alignment / stride)";
+        return cudaErrorInvalidValue;
+    }
+    KParams kp{};
+    kp.Mk = g.rows;
+    kp.Nk = g.N;
+    kp.K = g.K;
+    kp.tiles_m = 0;  // per group, from the device counts
+    kp.tiles_n = (g.N + BN - 1) / BN;
+    kp.k_blocks = (g.K + kTileK_Grouped - 1) / kTileK_Grouped;
+    kp.dp_tiles = 0;
+    kp.ctas = num_sms ? num_sms : 148;
+    kp.sk_iters = 0;
+    kp.c = g.c;
+    kp.ldc = g.ldc;
+    kp.c_type = g.c_type;
+    const uint32_t esz = g.c_type == 2 ? 4 : 2;
+    kp.vec_store_ok = ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0) && ((g.ldc * esz) % 16 == 0);
+    kp.row_scale_vec = g.row_scale_vec;
+    kp.col_scale_vec = g.col_scale_vec;
+    kp.row_scale = g.row_scale;
+    kp.col_scale = g.col_scale;
+    kp.raster_group = 1;
+    kp.grp_start = g.group_start;
+    kp.grp_count = g.group_count;
+    kp.groups = g.groups;
+    return launch_tile<BN, kTileK_Grouped, true>(ta, tb, kp, st);
 }
 
 // --------------------------------------------------------------------------

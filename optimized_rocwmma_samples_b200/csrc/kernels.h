@@ -70,6 +70,33 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
 cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* workspace, cudaStream_t st,
                            const char** detail);
 
+// Grouped (MoE) GEMM: group g multiplies A rows [group_start[g], +group_count[g])
+// (K-major, row-major [rows, K]) by B_g = rows [g*N, (g+1)*N) of a K-major
+// [groups*N, K] weight array; C rows follow A rows.  Counts live on the device.
+constexpr uint32_t kMaxGroups = 1024;
+struct GroupedProblem {
+    uint32_t groups, rows, N, K;
+    const int8_t* a;
+    uint32_t lda;
+    const int8_t* b;
+    uint32_t ldb;
+    void* c;
+    uint32_t ldc;
+    int c_type;
+    const float* row_scale_vec;
+    const float* col_scale_vec;  // [groups * N] or null
+    float row_scale, col_scale;
+    const int32_t* group_start;
+    const int32_t* group_count;
+};
+cudaError_t launch_gemm_i8_grouped(const GroupedProblem& g, uint32_t num_sms, cudaStream_t st, const char** detail);
+
+// MoE sorting (one CTA); shared memory it needs for `experts`.
+size_t moe_sort_smem(uint32_t experts);
+cudaError_t launch_moe_sort(const int32_t* ids, uint32_t tokens, uint32_t topk, uint32_t experts, uint32_t unit_size,
+                            int32_t* expert_count, int32_t* expert_start, int32_t* sorted_ids, int32_t* row_perm,
+                            cudaStream_t st);
+
 // Debug: a kernel that waits for an mbarrier nobody arrives on, with a limit.
 cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st);
 

@@ -126,3 +126,50 @@ def gemm_quant(a, b, sa_row=None, sb_col=None, scale_a=1.0, scale_b=1.0, out_dty
     """(acc int32, out uint16 bits) of the full reference-style quantized GEMM."""
     acc = gemm_i8_acc(a, b)
     return acc, dequant(acc, sa_row, sb_col, scale_a, scale_b, out_dtype)
+
+
+def moe_sorting(topk_ids, experts: int, unit_size: int = 1):
+    """rocwmma_moe_sorting.cpp:53-125 restated: histogram of valid expert ids,
+    exclusive prefix of counts padded to unit_size, scatter of token ids into
+    each expert's segment.  The reference's scatter order inside a segment is
+    whatever its atomics produce; this restatement uses the stable order
+    (increasing flat index).  Padding slots hold the sentinel `tokens`."""
+    ids = np.ascontiguousarray(topk_ids, dtype=np.int32)
+    T, K = ids.shape
+    flat = ids.reshape(-1)
+    valid = (flat >= 0) & (flat < experts)
+    count = np.bincount(flat[valid], minlength=experts).astype(np.int32)
+    padded = ((count + unit_size - 1) // unit_size) * unit_size
+    start = np.zeros(experts + 1, np.int32)
+    start[1:] = np.cumsum(padded)
+    sorted_ids = np.full(T * K + experts * unit_size, T, np.int32)
+    row_perm = np.full(T * K, -1, np.int32)
+    nxt = start[:-1].copy()
+    for f in range(T * K):
+        e = flat[f]
+        if 0 <= e < experts:
+            sorted_ids[nxt[e]] = f // K
+            row_perm[f] = nxt[e]
+            nxt[e] += 1
+    return count, start, sorted_ids, row_perm
+
+
+def gemm_grouped(a, w, start, count, sa_row=None, sb_col=None, out_dtype="bf16"):
+    """Per-group restatement: rows [start[g], start[g]+count[g]) of a times
+    w[g] ([N, K] K-major).  Returns (acc int32 [rows, N], out uint16 bits);
+    rows outside every group are zero."""
+    rows, K = a.shape
+    E, N, _ = w.shape
+    acc = np.zeros((rows, N), np.int32)
+    out = np.zeros((rows, N), np.uint16)
+    for g in range(E):
+        r0, n = int(start[g]), int(count[g])
+        if n == 0:
+            continue
+        ag = np.ascontiguousarray(a[r0:r0 + n])
+        acc_g = gemm_i8_acc(ag, w[g].T)
+        acc[r0:r0 + n] = acc_g
+        sa = None if sa_row is None else sa_row[r0:r0 + n]
+        sb = None if sb_col is None else sb_col[g * N:(g + 1) * N]
+        out[r0:r0 + n] = dequant(acc_g, sa, sb, out_dtype=out_dtype)
+    return acc, out

@@ -130,3 +130,20 @@ def test_plan_choices():
     assert p.dp_tiles == 0 and p.sk_iters == 380 * p.k_blocks  # 2.6 rounds: all stream-K
     p = api.plan(8192, 8192, 8192, api.ROW_MAJOR, api.ROW_MAJOR, num_sms=148)
     assert p.tile_n in (128, 256)
+
+
+def test_moe_entry_points_validation_without_gpu():
+    lib = _lib.load()
+    buf = (C.c_int32 * 64)()
+    p = C.addressof(buf)
+    assert lib.b2sq_moe_sorting(p, 4, 2, 0, 1, p, p, p, p, None) == _lib.B2SQ_ERR_INVALID_ARG  # no experts
+    assert lib.b2sq_moe_sorting(p, 4, 2, 2000, 1, p, p, p, p, None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_moe_sorting(p, 4, 2, 8, 0, p, p, p, p, None) == _lib.B2SQ_ERR_INVALID_ARG  # unit_size 0
+    assert lib.b2sq_gemm_i8_grouped(0, 16, 16, 16, p, 16, p, 16, p, 1, 16, None, None, 1, 1, p, p,
+                                    None) == _lib.B2SQ_OK  # no groups: no-op
+    assert lib.b2sq_gemm_i8_grouped(2, 16, 16, 16, p, 16, p, 16, p, 7, 16, None, None, 1, 1, p, p,
+                                    None) == _lib.B2SQ_ERR_INVALID_ARG  # dtype
+    assert lib.b2sq_gemm_i8_grouped(2, 16, 16, 16, p, 8, p, 16, p, 1, 16, None, None, 1, 1, p, p,
+                                    None) == _lib.B2SQ_ERR_INVALID_ARG  # lda < k
+    assert lib.b2sq_gemm_i8_grouped(2, 16, 16, 24, (p + 15) & ~15, 24, (p + 15) & ~15, 32, p, 1, 16, None, None, 1, 1,
+                                    p, p, None) == _lib.B2SQ_ERR_UNSUPPORTED  # lda % 16

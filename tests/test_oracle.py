@@ -182,3 +182,13 @@ def test_golden_c1_fixture():
     # the fixture is also internally consistent with the numpy restatement
     y2, rs2 = np_smoothquant(g["x"], g["smooth"])
     assert np.array_equal(g["y"], y2) and np.array_equal(g["row_scale"], rs2)
+
+
+def test_kat_moe_sorting():
+    # 4 tokens, top-2, 3 experts, unit_size 4; id -1 and 5 are invalid (rocwmma_moe_sorting.cpp:70, :120)
+    ids = np.array([[0, 2], [2, 1], [-1, 2], [0, 5]], np.int32)
+    cnt, start, sids, perm = O.moe_sorting(ids, 3, 4)
+    assert list(cnt) == [2, 1, 3]
+    assert list(start) == [0, 4, 8, 12]  # counts padded to 4 (:93-96), sentinel total at [E]
+    assert list(sids[:12]) == [0, 3, 4, 4, 1, 4, 4, 4, 0, 1, 2, 4]  # padding slots hold `tokens` (4)
+    assert list(perm) == [0, 8, 9, 4, -1, 10, 1, -1]
