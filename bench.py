@@ -298,6 +298,70 @@ def main():
     sq_gbs = sq_bytes / (sq_ms * 1e-3) / 1e9
     del x, y
 
+    def timed(fn, n):
+        """Mean device ms of fn over n steps (L2 flushed before each), max over ranks."""
+        for _ in range(3):
+            fn()
+        evs = []
+        barrier()
+        for _ in range(n):
+            l2_flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        t_ = torch.tensor([statistics.mean(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        return float(t_.item())
+
+    # ---------------- config 3: decode smoothquant + GEMM, HBM bound
+    decode = {}
+    w_dec = synth.torch_int8_uniform((28672, K), dev, 31)
+    sb_dec = synth.torch_scales(28672, dev, 32)
+    s_dec = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
+    for md in (16, 64):
+        x_dec = torch.randn((md, K), generator=g, device=dev).to(torch.float16)
+        y_dec = torch.empty((md, K), dtype=torch.int8, device=dev)
+        r_dec = torch.empty((md,), dtype=torch.float32, device=dev)
+        o_dec = torch.empty((md, 28672), dtype=torch.float16, device=dev)
+
+        def dec_step():
+            api.smoothquant(x_dec, s_dec, y=y_dec, row_scale=r_dec)
+            api.gemm_quant(y_dec, w_dec.t(), r_dec, sb_dec, out_dtype=torch.float16, c=o_dec, workspace=ws)
+
+        ms_d = timed(dec_step, 50)
+        bytes_d = (md * K * 2 + md * K + K * 4 + md * 4) + (md * K + 28672 * K + 4 * 28672 + 4 * md + 2 * md * 28672)
+        decode[f"m{md}"] = {"ms": ms_d, "gbs": world * bytes_d / (ms_d * 1e-3) / 1e9,
+                            "frac_of_measured_hbm": bytes_d / (ms_d * 1e-3) / 1e9 / hbm_gbs,
+                            "shape": [md, K, 28672], "gpu_launches_per_step": 2}
+    del w_dec
+
+    # ---------------- config 4: N-sharded prefill (smoothquant + GEMM), 16384 x 8192 x 28672
+    from optimized_rocwmma_samples_b200.sharded import ShardedPrefill, cuda_ops, shard_range
+
+    PM, PN = 16384, 28672
+    n0, n1 = shard_range(PN, world, rank)
+    w_pf = synth.torch_int8_uniform((n1 - n0, K), dev, 40 + rank)
+    sb_pf = synth.torch_scales(n1 - n0, dev, 50 + rank)
+    layer = ShardedPrefill(w_pf, sb_pf, PN, cuda_ops(torch.bfloat16))
+    x_pf = torch.randn((PM, K), generator=g, device=dev).to(torch.float16)
+    s_pf = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
+    ops_pf = 2.0 * PM * PN * K
+    ms_pf = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", False), 10)
+    prefill = {"shape": [PM, K, PN], "shard_cols": n1 - n0,
+               "sharded_compute": {"ms": ms_pf, "tops": ops_pf / (ms_pf * 1e-3) / 1e12,
+                                   "note": "x replicated, each rank quantises and multiplies its N shard, "
+                                           "output left N-sharded"}}
+    if world > 1:
+        ms_e = timed(lambda: layer.forward(x_pf if rank == 0 else None, s_pf, PM, K, "rank0", True), 5)
+        prefill["with_collectives"] = {"ms": ms_e, "tops": ops_pf / (ms_e * 1e-3) / 1e12,
+                                       "note": "rank 0 quantises, NCCL broadcast of Xq and row scales, "
+                                               "sharded GEMM, NCCL all-gather of the bf16 output into [M, N]"}
+    del layer, w_pf, x_pf
+
     # ---------------- e2e through the C ABI from pinned host buffers
     h_a = a.cpu().pin_memory()
     h_w = w.cpu().pin_memory()
@@ -357,6 +421,8 @@ def main():
                                       f"nominal int8 4500 TOPS -> frac {achieved / 4500.0:.3f}"},
             "smoothquant": {"shape": [SQ_M, SQ_K], "ms": sq_ms, "gbs": sq_gbs,
                             "frac_of_measured_hbm": sq_gbs / hbm_gbs, "hbm_peak_gbs": hbm_gbs},
+            "decode": decode,
+            "prefill_c4": prefill,
             "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
