@@ -139,12 +139,12 @@ B2SQ_API b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k,
  * reference): for callers that cannot allocate device memory, e.g. a host
  * bound over a plain C FFI with no device allocator, or a serving process
  * that has given all of HBM to its own pool and must not call cudaMalloc on
- * the request path.  The stream-K scratch comes from a fixed 16 MiB array
+ * the request path.  The stream-K scratch comes from a fixed 24 MiB array
  * compiled into the library, resident on every GPU that loads it until the
  * process exits; nothing is allocated.  Shapes whose schedule needs more
  * scratch than that return B2SQ_ERR_UNSUPPORTED (use b2sq_gemm_i8 with a
- * workspace); all skinny-M (M <= 64) decode shapes and every shape without
- * stream-K fit.  Arguments and results are those of b2sq_gemm_i8.
+ * workspace); every shape whose tiles are at most 128 wide fits, and so
+ * does every shape whose schedule needs no stream-K.  Arguments and results are those of b2sq_gemm_i8.
  * The first call on a device looks up the array's device address (once per
  * device); make that first call before any stream capture.  Every call
  * shares the array and clears its counters itself: calls that overlap on the

@@ -922,7 +922,12 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
     const uint64_t T = (uint64_t)s.tiles_m * s.tiles_n;
     const uint64_t rounds = (T + P - 1) / P;
     const double tail_loss = (double)(rounds * P - T) / (double)(rounds * P);
-    if (!allow_stream_k || s.k_blocks < 2 || tail_loss <= kStreamKMinTailLoss) {
+    // Skinny tiles (tile_n <= 64, the decode shapes) are bound by HBM: when
+    // part of the SMs run out of tiles the others take over the bandwidth, so
+    // splitting tiles gains nothing and its fix-up costs a few microseconds
+    // (measured).  Stream-K is for compute-bound tails.
+    const bool hbm_bound = bn <= 64;
+    if (!allow_stream_k || hbm_bound || s.k_blocks < 2 || tail_loss <= kStreamKMinTailLoss) {
         s.dp_tiles = (uint32_t)T;
         s.sk_iters = 0;
         s.ctas = (uint32_t)(T < P ? T : P);

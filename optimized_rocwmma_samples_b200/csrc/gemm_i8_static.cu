@@ -20,10 +20,10 @@
 
 namespace {
 
-// Largest stream-K scratch a call may need.  16 MiB covers every skinny-M
-// (decode) shape, whose tiles are at most 64 wide, and every shape whose
-// schedule needs no stream-K; larger needs are rejected.
-constexpr size_t kStaticScratchBytes = 16u << 20;
+// Largest stream-K scratch a call may need.  24 MiB covers every shape whose
+// tiles are at most 128 wide (148 SMs) and every shape whose schedule needs
+// no stream-K; larger needs (256-wide stream-K tiles) are rejected.
+constexpr size_t kStaticScratchBytes = 24u << 20;
 
 static __device__ __align__(256) unsigned char g_gemm_scratch[kStaticScratchBytes];
 

@@ -119,7 +119,10 @@ def test_schedule_covers_each_kblock_once(m, n, k, sk):
 
 def test_plan_choices():
     p = api.plan(16, 28672, 8192, num_sms=148)
-    assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 0  # all stream-K
+    # decode: skinny tiles are HBM-bound, whole tiles only (no stream-K)
+    assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 224 and p.sk_iters == 0
+    p = api.plan(100, 4096, 4096, num_sms=148)
+    assert p.swap_ab == 1 and p.tile_n == 128 and p.dp_tiles == 0  # compute-bound small problem: all stream-K
     p = api.plan(8192, 8192, 8192, num_sms=148)
     # CTA pairs: 1024 tiles of 256 x 256 over 74 pairs, 14 rounds, 1.2% idle
     assert p.cta_pair == 1 and p.swap_ab == 0 and p.tile_m == 256 and p.tile_n == 256

@@ -40,7 +40,9 @@ def no_alloc(a, w, sa, sb, out_dtype):
     return st, c
 
 
-@pytest.mark.parametrize("M,N,K", [(16, 28672, 8192), (64, 28672, 4096), (200, 64, 2048), (8192, 8192, 1024)])
+# (100, 4096, 4096): swapped 128-wide tiles, all stream-K (~19 MiB of scratch);
+# (16, 28672, 8192): decode, no scratch needed; (8192, 8192, 1024): whole tiles.
+@pytest.mark.parametrize("M,N,K", [(100, 4096, 4096), (16, 28672, 8192), (8192, 8192, 1024)])
 def test_no_alloc_matches_workspace_entry_point(cuda_device, M, N, K):
     dev = cuda_device
     for call in range(2):  # two calls in a row share (and must re-clear) the scratch
@@ -63,13 +65,13 @@ def test_no_alloc_matches_workspace_entry_point(cuda_device, M, N, K):
 
 
 def test_no_alloc_rejects_oversized_scratch(cuda_device):
-    # m = 100 -> swapped 128-wide tiles, all stream-K: needs ~19 MiB of scratch (> 16 MiB)
+    # 2048^3: 64 tiles of 128 x 256 over 148 SMs, all stream-K: ~39 MiB of scratch (> 24 MiB)
     dev = cuda_device
-    a = synth.torch_int8_uniform((100, 4096), dev, 1)
-    w = synth.torch_int8_uniform((4096, 4096), dev, 2)
-    sa, sb = synth.torch_scales(100, dev, 3), synth.torch_scales(4096, dev, 4)
-    need = api.workspace_size(100, 4096, 4096)
-    assert need > 16 << 20
+    a = synth.torch_int8_uniform((2048, 2048), dev, 1)
+    w = synth.torch_int8_uniform((2048, 2048), dev, 2)
+    sa, sb = synth.torch_scales(2048, dev, 3), synth.torch_scales(2048, dev, 4)
+    need = api.workspace_size(2048, 2048, 2048)
+    assert need > 24 << 20
     st, _ = no_alloc(a, w, sa, sb, torch.float16)
     assert st == _lib.B2SQ_ERR_UNSUPPORTED
     assert b"scratch" in _lib.load().b2sq_last_error_message()
