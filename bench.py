@@ -328,9 +328,9 @@ def main():
         r_dec = torch.empty((md,), dtype=torch.float32, device=dev)
         o_dec = torch.empty((md, 28672), dtype=torch.float16, device=dev)
 
-        def dec_step():
-            api.smoothquant(x_dec, s_dec, y=y_dec, row_scale=r_dec)
-            api.gemm_quant(y_dec, w_dec.t(), r_dec, sb_dec, out_dtype=torch.float16, c=o_dec, workspace=ws)
+        def dec_step():  # one fused call: smoothquant, then the GEMM launched with PDL
+            api.smoothquant_gemm(x_dec, s_dec, w_dec, sb_dec, out_dtype=torch.float16, xq=y_dec, row_scale=r_dec,
+                                 c=o_dec, workspace=ws)
 
         ms_d = timed(dec_step, 50)
         bytes_d = (md * K * 2 + md * K + K * 4 + md * 4) + (md * K + 28672 * K + 4 * 28672 + 4 * md + 2 * md * 28672)

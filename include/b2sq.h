@@ -158,6 +158,25 @@ B2SQ_API b2sq_status b2sq_gemm_i8_no_alloc(uint32_t m, uint32_t n, uint32_t k,
                                            float scale_a, float scale_b,
                                            b2sq_stream_t stream);
 
+/*
+ * The whole hot path in one call: b2sq_smoothquant of x [m, k] (fp16) into
+ * xq / row_scale (caller-owned, [m, k] int8 and [m] fp32), then
+ *   c = cvt_rn(float(xq @ w) * (row_scale[i] * sw))
+ * with w [k, n] (column-major = K-major [n, k] weights, or row-major) and
+ * sw = scale_w_col ? scale_w_col[j] : scale_w; c f16 or bf16, row-major.
+ * Results are identical to the two separate calls.  The GEMM is enqueued
+ * with programmatic dependent launch: its prologue and the streaming of the
+ * weights overlap the smoothquant kernel, which matters for decode-sized m
+ * (the survey's "fuse smoothquant into the GEMM producer" row).  k % 16 == 0.
+ */
+B2SQ_API b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* smooth_scale, float quant_max,
+                                              int8_t* xq, float* row_scale, uint32_t m, uint32_t k,
+                                              const int8_t* w, b2sq_layout lw, uint32_t ldw, uint32_t n,
+                                              void* c, b2sq_dtype c_type, uint32_t ldc,
+                                              const float* scale_w_col, float scale_w,
+                                              void* workspace, size_t workspace_bytes,
+                                              b2sq_stream_t stream);
+
 /* Bytes of workspace that let b2sq_gemm_i8 use stream-K for this shape
  * (0 when the chosen schedule never splits a tile).  Host only. */
 B2SQ_API b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k,

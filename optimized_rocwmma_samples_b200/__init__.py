@@ -19,6 +19,7 @@ from .api import (  # noqa: F401
     moe_sorting,
     plan,
     smoothquant,
+    smoothquant_gemm,
     workspace_size,
 )
 

@@ -269,3 +269,33 @@ def gemm_grouped(a: torch.Tensor, w: torch.Tensor, group_start: torch.Tensor, gr
                                   group_count.data_ptr(), _stream_ptr(stream, dev))
     _lib.check(st, "b2sq_gemm_i8_grouped")
     return c
+
+
+def smoothquant_gemm(x: torch.Tensor, smooth_scale: torch.Tensor, w_nk: torch.Tensor,
+                     scale_w_col: Optional[torch.Tensor] = None, scale_w: float = 1.0, quant_max: float = 127.0,
+                     out_dtype: torch.dtype = torch.float16, xq: Optional[torch.Tensor] = None,
+                     row_scale: Optional[torch.Tensor] = None, c: Optional[torch.Tensor] = None,
+                     workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None):
+    """Smoothquant of x [M, K] followed by the int8 GEMM with K-major weights
+    w_nk [N, K], in one C-ABI call (the GEMM is launched with programmatic
+    dependent launch).  Returns (c, xq, row_scale)."""
+    if x.dtype != torch.float16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous fp16 [M, K] tensor")
+    M, K = x.shape
+    if w_nk.dtype != torch.int8 or w_nk.dim() != 2 or w_nk.shape[1] != K or w_nk.stride(1) != 1:
+        raise ValueError("w_nk must be int8 [N, K] with unit stride along K")
+    N = w_nk.shape[0]
+    xq = torch.empty((M, K), dtype=torch.int8, device=x.device) if xq is None else xq
+    row_scale = torch.empty((M,), dtype=torch.float32, device=x.device) if row_scale is None else row_scale
+    c = torch.empty((M, N), dtype=out_dtype, device=x.device) if c is None else c
+    dev = _need_cuda(x, smooth_scale, w_nk, xq, row_scale, c, scale_w_col)
+    need = workspace_size(M, N, K, ROW_MAJOR, COL_MAJOR)
+    ws = (workspace or _default_ws).get(dev, need)
+    lib = _lib.load()
+    st = lib.b2sq_smoothquant_gemm_i8(x.data_ptr(), smooth_scale.data_ptr(), float(quant_max), xq.data_ptr(),
+                                      row_scale.data_ptr(), M, K, w_nk.data_ptr(), COL_MAJOR, w_nk.stride(0), N,
+                                      c.data_ptr(), _DTYPE_CODE[out_dtype], c.stride(0), _ptr(scale_w_col),
+                                      float(scale_w), _ptr(ws), 0 if ws is None else ws.numel(),
+                                      _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_smoothquant_gemm_i8")
+    return c, xq, row_scale

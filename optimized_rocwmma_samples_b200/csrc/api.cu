@@ -227,10 +227,16 @@ b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k, b2sq
     return ok();
 }
 
-b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
+}  // extern "C"
+
+namespace {
+// Body of b2sq_gemm_i8.  a_from_prev_kernel: the A operand and scale_a_row
+// are written by the kernel enqueued just before on the same stream; the GEMM
+// is then launched with programmatic dependent launch.
+b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
                          const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
                          const float* scale_a_row, const float* scale_b_col, float scale_a, float scale_b,
-                         void* workspace, size_t workspace_bytes, b2sq_stream_t stream)
+                         void* workspace, size_t workspace_bytes, b2sq_stream_t stream, bool a_from_prev_kernel)
 {
     b2sq_status st = validate_gemm(m, n, k, a, la, lda, b, lb, ldb, c, c_type, ldc, scale_a_row, scale_b_col);
     if (st != B2SQ_OK || m == 0 || n == 0) return st;
@@ -256,6 +262,7 @@ b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
     p.ldc = ldc;
     p.c_type = (int)c_type;
     p.transpose_out = (int)mp.swap;
+    p.pdl_dep = a_from_prev_kernel ? (mp.swap ? 2 : 1) : 0;
     if (mp.swap) {
         p.a = b;
         p.lda = ldb;
@@ -288,6 +295,34 @@ b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
         return cuda_fail(e, "gemm_i8 launch");
     }
     return ok();
+}
+}  // namespace
+
+extern "C" {
+
+b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
+                         const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
+                         const float* scale_a_row, const float* scale_b_col, float scale_a, float scale_b,
+                         void* workspace, size_t workspace_bytes, b2sq_stream_t stream)
+{
+    return gemm_i8_impl(m, n, k, a, la, lda, b, lb, ldb, c, c_type, ldc, scale_a_row, scale_b_col, scale_a, scale_b,
+                        workspace, workspace_bytes, stream, false);
+}
+
+b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* smooth_scale, float quant_max, int8_t* xq,
+                                     float* row_scale, uint32_t m, uint32_t k, const int8_t* w, b2sq_layout lw,
+                                     uint32_t ldw, uint32_t n, void* c, b2sq_dtype c_type, uint32_t ldc,
+                                     const float* scale_w_col, float scale_w, void* workspace, size_t workspace_bytes,
+                                     b2sq_stream_t stream)
+{
+    if (c_type == B2SQ_I32) return fail(B2SQ_ERR_INVALID_ARG, "smoothquant_gemm_i8: output must be f16 or bf16");
+    if (m == 0 || n == 0) return ok();
+    if (k % 16) return fail(B2SQ_ERR_UNSUPPORTED, "smoothquant_gemm_i8: k must be a multiple of 16 (TMA)");
+    if (!aligned(xq, 16)) return fail(B2SQ_ERR_UNSUPPORTED, "smoothquant_gemm_i8: xq must be 16-byte aligned");
+    b2sq_status st = b2sq_smoothquant(x_f16, smooth_scale, xq, row_scale, m, k, quant_max, stream);
+    if (st != B2SQ_OK) return st;
+    return gemm_i8_impl(m, n, k, xq, B2SQ_ROW_MAJOR, k, w, lw, ldw, c, c_type, ldc, row_scale, scale_w_col, 1.f,
+                        scale_w, workspace, workspace_bytes, stream, true);
 }
 
 b2sq_status b2sq_moe_sorting(const int32_t* topk_ids, uint32_t tokens, uint32_t topk, uint32_t experts,

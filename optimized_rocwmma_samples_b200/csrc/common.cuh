@@ -209,6 +209,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL)
+// ---------------------------------------------------------------------------
+// Waits until the kernel this one depends on has completed and its memory is
+// visible (returns at once when the launch had no programmatic dependency).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets a kernel launched after this one with PDL start its prologue now.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // CTA pairs (thread-block clusters of 2) for cta_group::2 MMAs.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank()

@@ -97,6 +97,9 @@ struct KParams {
     const int32_t* grp_start;
     const int32_t* grp_count;
     uint32_t groups;
+    // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
+    // row scales) are written by the kernel launched just before this one.
+    uint32_t pdl_dep;
 };
 
 constexpr uint32_t kTileK_Grouped = tile_k_for(256);
@@ -397,12 +400,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued_phase[8];
             bool issued[8];
             for (uint32_t s = 0; s < 8; ++s) issued[s] = false, issued_phase[s] = 0;
+            // One stage's A / B tiles (BK/128 swizzle atoms along K each).
+            auto load_a = [&](uint32_t sa, uint32_t fb, uint32_t kb, int32_t a_row) {
+#pragma unroll
+                for (uint32_t i = 0; i < KATOMS; ++i) {
+                    const int32_t kc = (int32_t)(kb * BK + i * 128);
+                    // K-major: atom i is [128 rows][128 B]; MN-major: k rows are contiguous.
+                    if (p.a_mn_major) tma_load_2d(sa + i * (128 * 128), &tmA, fb, a_row, kc);
+                    else tma_load_2d(sa + i * (kTileM * 128), &tmA, fb, kc, a_row);
+                }
+            };
+            auto load_b = [&](uint32_t sb, uint32_t fb, uint32_t kb, int32_t b_row) {
+#pragma unroll
+                for (uint32_t i = 0; i < KATOMS; ++i) {
+                    const int32_t kc = (int32_t)(kb * BK + i * 128);
+                    if (p.b_mn_major) {
+#pragma unroll
+                        for (uint32_t j = 0; j < BN / 128; ++j)
+                            tma_load_2d(sb + j * (BK * 128) + i * (128 * 128), &tmB, fb, b_row + (int32_t)(j * 128), kc);
+                    } else {
+                        tma_load_2d(sb + i * (BN * 128), &tmB, fb, kc, b_row);
+                    }
+                }
+            };
+            // Programmatic dependent launch: the operand written by the
+            // previous kernel (p.pdl_dep: 1 = A, 2 = B) is loaded only after
+            // griddepcontrol.wait; the other operand of the first ring of
+            // stages is already streaming meanwhile.
+            bool pdl_pending = p.pdl_dep != 0;
+            uint32_t ndef = 0, def_stage[8], def_kb[8];
+            int32_t def_row[8];
+            auto flush_deferred = [&]() {
+                griddep_wait();
+                for (uint32_t d = 0; d < ndef; ++d) {
+                    const uint32_t sa = sbase + def_stage[d] * L::SB;
+                    const uint32_t fb = full_bar + 8 * def_stage[d];
+                    if (p.pdl_dep == 1) load_a(sa, fb, def_kb[d], def_row[d]);
+                    else load_b(sa + L::A_BYTES, fb, def_kb[d], def_row[d]);
+                }
+                ndef = 0;
+                pdl_pending = false;
+            };
             bool ok = true;
             while (ok && it.next(p, u)) {
                 const TileGeom tg = tile_geom<kGrouped, BN>(p, u.tile, gpre);
                 const int32_t a_row = (int32_t)tg.a_row;
                 const int32_t b_row = (int32_t)tg.b_row;
                 for (uint32_t kb = u.k0; kb < u.k1; ++kb) {
+                    if (pdl_pending && ndef == ST) flush_deferred();  // the ring is full of half-loaded stages
                     if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
                         ok = false;
                         break;
@@ -411,26 +456,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(fb, L::SB);
                     const uint32_t sa = sbase + stage * L::SB;
                     const uint32_t sb = sa + L::A_BYTES;
-#pragma unroll
-                    for (uint32_t i = 0; i < KATOMS; ++i) {
-                        const int32_t kc = (int32_t)(kb * BK + i * 128);
-                        // K-major: atom i is [128 rows][128 B]; MN-major: k rows are contiguous.
-                        if (p.a_mn_major) tma_load_2d(sa + i * (128 * 128), &tmA, fb, a_row, kc);
-                        else tma_load_2d(sa + i * (kTileM * 128), &tmA, fb, kc, a_row);
-                        if (p.b_mn_major) {
-#pragma unroll
-                            for (uint32_t j = 0; j < BN / 128; ++j)
-                                tma_load_2d(sb + j * (BK * 128) + i * (128 * 128), &tmB, fb, b_row + (int32_t)(j * 128),
-                                            kc);
-                        } else {
-                            tma_load_2d(sb + i * (BN * 128), &tmB, fb, kc, b_row);
-                        }
+                    if (!pdl_pending) {
+                        load_a(sa, fb, kb, a_row);
+                        load_b(sb, fb, kb, b_row);
+                    } else {
+                        if (p.pdl_dep == 1) load_b(sb, fb, kb, b_row);
+                        else load_a(sa, fb, kb, a_row);
+                        def_stage[ndef] = stage;
+                        def_kb[ndef] = kb;
+                        def_row[ndef] = p.pdl_dep == 1 ? a_row : b_row;
+                        ++ndef;
                     }
                     issued[stage] = true;
                     issued_phase[stage] = phase;
                     if (++stage == ST) stage = 0, phase ^= 1;
                 }
             }
+            if (pdl_pending) flush_deferred();
             // Drain: every TMA copy this thread issued lands before the CTA
             // exits (immediate on the normal path).
             for (uint32_t s = 0; s < ST; ++s)
@@ -486,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();  // reconverge before the CTA-wide barrier below
     } else {
         // ------------------------------------------------------------ epilogue
+        if (p.pdl_dep) griddep_wait();  // row scales come from the previous kernel
         const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
         const uint32_t row_local = q * 32 + lane;
         const uint32_t ethread = threadIdx.x - 64;
@@ -862,6 +905,19 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
+    if (kp.pdl_dep) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(kp.ctas);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = L::total;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped>, ta, tb, kp, (uint64_t)kWaitLimitNs);
+    }
     gemm_i8_kernel<BN, BK, kGrouped><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
@@ -989,6 +1045,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
         kp.ws_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
     }
     kp.raster_group = B2SQ_RASTER_GROUP;
+    kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
     if (s.cta_pair) return launch_pair(ta, tb, kp, st);
     switch (bn) {

@@ -32,6 +32,7 @@ struct GemmProblem {
     const float* row_scale_vec;  // per kernel-row scale (nullable)
     const float* col_scale_vec;  // per kernel-column scale (nullable)
     float row_scale, col_scale;  // used when the vector is null
+    int pdl_dep;                 // 1 / 2: A / B (and row scales) come from the previous kernel (PDL)
 };
 
 struct GemmSchedule {

@@ -219,6 +219,7 @@ __global__ void __launch_bounds__(kThreads) sq_vec_kernel(const __half* __restri
                                                           int8_t* __restrict__ y, float* __restrict__ row_scale,
                                                           uint32_t M, uint32_t N, float qmax)
 {
+    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
     __shared__ float red[kThreads / 32];
     constexpr int R = kThreads / G;
     const int lane_in_group = threadIdx.x % G;
@@ -264,6 +265,7 @@ __global__ void __launch_bounds__(kThreads) moe_sq_vec_kernel(const __half* __re
                                                               uint32_t experts, float qmax,
                                                               const int32_t* __restrict__ row_perm)
 {
+    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
     __shared__ float red[2][kThreads / 32];
     constexpr int R = kThreads / G;
     const int lane_in_group = threadIdx.x % G;
@@ -516,6 +518,7 @@ __global__ void __launch_bounds__(kTmaThreads) sq_tma_kernel(const __half* __res
                                                              uint32_t M, uint32_t N, float qmax, uint32_t stages,
                                                              uint32_t stage_bytes, uint32_t out_bytes)
 {
+    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
     extern __shared__ __align__(128) uint8_t smem[];
     const TmaRing r = tma_ring(smem, stages, stage_bytes);
     const uint32_t out_base = r.data + stages * stage_bytes + kTmaReserved;
@@ -569,6 +572,7 @@ __global__ void __launch_bounds__(kTmaThreads) moe_sq_tma_kernel(const __half* _
                                                                  float qmax, const int32_t* __restrict__ row_perm,
                                                                  uint32_t stages, uint32_t stage_bytes, uint32_t out_bytes)
 {
+    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
     extern __shared__ __align__(128) uint8_t smem[];
     const TmaRing r = tma_ring(smem, stages, stage_bytes);
     const uint32_t out_base = r.data + stages * stage_bytes + kTmaReserved;
@@ -646,6 +650,7 @@ __global__ void __launch_bounds__(kThreads) sq_generic_kernel(const __half* __re
                                                               int8_t* __restrict__ y, float* __restrict__ row_scale,
                                                               uint32_t M, uint32_t N, float qmax)
 {
+    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
     __shared__ float red[kThreads / 32];
     for (uint64_t row = blockIdx.x; row < M; row += gridDim.x)
         sq_row_generic(x + row * N, smooth, y + row * N, row_scale + row, N, qmax, red);
@@ -659,6 +664,7 @@ __global__ void __launch_bounds__(kThreads) moe_sq_generic_kernel(const __half* 
                                                                   uint32_t hidden, uint32_t topk, uint32_t experts,
                                                                   float qmax, const int32_t* __restrict__ row_perm)
 {
+    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
     __shared__ float red[kThreads / 32];
     const uint64_t total = (uint64_t)tokens * topk;
     for (uint64_t flat = blockIdx.x; flat < total; flat += gridDim.x) {
