@@ -47,7 +47,7 @@ def _sources() -> list[Path]:
 
 
 def _deps() -> list[Path]:
-    return _sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
+    return _sources() + [PKG / "samples" / "b2sq_samples.cpp"] + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:
@@ -85,7 +85,24 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if res.returncode != 0:
         raise RuntimeError(f"link of libb2sq.so failed:\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, LIB)
+    build_samples(verbose)
     return LIB
+
+
+SAMPLES_SRC = PKG / "samples" / "b2sq_samples.cpp"
+SAMPLES_BIN = PKG / "b2sq_samples"
+
+
+def build_samples(verbose: bool = False) -> Path:
+    """The C++ host driver mirroring the reference samples (links libb2sq.so)."""
+    cmd = [nvcc(), *ARCH, "-O2", "-std=c++17", f"-I{INCLUDE}", "-o", str(SAMPLES_BIN), str(SAMPLES_SRC),
+           f"-L{PKG}", "-lb2sq", "-Xlinker", "-rpath=$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"build of b2sq_samples failed:\n{res.stdout}\n{res.stderr}")
+    return SAMPLES_BIN
 
 
 if __name__ == "__main__":

@@ -1,0 +1,275 @@
+// b2sq_samples.cpp — host driver mirroring the reference samples' main()s on
+// top of libb2sq, with the same inputs, timing convention and output lines:
+//
+//   rocwmma_smoothquant.cpp:138-176      [SmoothQuant] M=.. N=..  X ms  Y GB/s
+//   rocwmma_moe_smoothquant.cpp:147-206  [MoE-SmoothQuant] tokens=.. ...  X ms  Y GB/s
+//   rocwmma_gemm_quantized.cpp:197-268   [QuantGEMM-I8] M=.. N=.. K=..  X ms  Y TFlops/s
+//   rocwmma_moe_sorting.cpp:141-208      [MoE-Sorting] tokens=.. experts=.. topk=.. unit=..  X ms
+//
+// so output parsers written for the reference (benchmark.sh:177-188) read it
+// unchanged.  Inputs are the reference drivers' constants (x = 0.5, smooth = 1,
+// A = B = 1 as int8 standing in for fp8(0.1)); timing: warm-up launches, then
+// timed launches bracketed by events (rocwmma_smoothquant.cpp:124-136).  Each
+// sample also checks the known answer its constant inputs imply and exits
+// non-zero on a mismatch (the reference checks nothing here).
+//
+//   b2sq_samples [smoothquant|moe|gemm|sorting|all] [M N]
+#include "../../include/b2sq.h"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <random>
+#include <set>
+#include <string>
+#include <utility>
+#include <vector>
+
+#define CHECK_CUDA(x)                                                                        \
+    do {                                                                                     \
+        cudaError_t e_ = (x);                                                                \
+        if (e_ != cudaSuccess) {                                                             \
+            std::fprintf(stderr, "CUDA %s at %s:%d\n", cudaGetErrorString(e_), __FILE__, __LINE__); \
+            std::exit(1);                                                                    \
+        }                                                                                    \
+    } while (0)
+#define CHECK_B2SQ(x)                                                                        \
+    do {                                                                                     \
+        b2sq_status s_ = (x);                                                                \
+        if (s_ != B2SQ_OK) {                                                                 \
+            std::fprintf(stderr, "b2sq %s: %s\n", b2sq_status_string(s_), b2sq_last_error_message()); \
+            std::exit(1);                                                                    \
+        }                                                                                    \
+    } while (0)
+
+static int g_failures = 0;
+
+template <typename Fn>
+static double bench(Fn fn, int warm = 5, int runs = 20)
+{
+    for (int i = 0; i < warm; ++i) fn();
+    CHECK_CUDA(cudaDeviceSynchronize());
+    cudaEvent_t t0, t1;
+    CHECK_CUDA(cudaEventCreate(&t0));
+    CHECK_CUDA(cudaEventCreate(&t1));
+    CHECK_CUDA(cudaEventRecord(t0));
+    for (int i = 0; i < runs; ++i) fn();
+    CHECK_CUDA(cudaEventRecord(t1));
+    CHECK_CUDA(cudaEventSynchronize(t1));
+    float ms = 0.f;
+    CHECK_CUDA(cudaEventElapsedTime(&ms, t0, t1));
+    CHECK_CUDA(cudaEventDestroy(t0));
+    CHECK_CUDA(cudaEventDestroy(t1));
+    return ms / runs;
+}
+
+static uint16_t half_of(float f)
+{
+    // 0.5 and 1.0 only: exact fp16 bit patterns.
+    return f == 0.5f ? 0x3800 : 0x3C00;
+}
+
+static void test_smoothquant(uint32_t M, uint32_t N)
+{
+    std::vector<uint16_t> hX((size_t)M * N, half_of(0.5f));
+    std::vector<float> hS(N, 1.f);
+    void* dX;
+    float *dS, *dRS;
+    int8_t* dY;
+    CHECK_CUDA(cudaMalloc(&dX, hX.size() * 2));
+    CHECK_CUDA(cudaMalloc(&dY, (size_t)M * N));
+    CHECK_CUDA(cudaMalloc(&dS, N * 4));
+    CHECK_CUDA(cudaMalloc(&dRS, M * 4));
+    CHECK_CUDA(cudaMemcpy(dX, hX.data(), hX.size() * 2, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dS, hS.data(), N * 4, cudaMemcpyHostToDevice));
+    auto fn = [&] { CHECK_B2SQ(b2sq_smoothquant(dX, dS, dY, dRS, M, N, 127.f, nullptr)); };
+    const double ms = bench(fn);
+    const double bw = ((double)M * N * 2 + (double)M * N + (double)N * 4 + (double)M * 4) / (ms * 1e-3) / 1e9;
+    std::printf("[SmoothQuant] M=%u N=%u  %g ms  %g GB/s\n", M, N, ms, bw);
+    std::vector<int8_t> hY((size_t)M * N);
+    float rs0 = 0.f;
+    CHECK_CUDA(cudaMemcpy(hY.data(), dY, hY.size(), cudaMemcpyDeviceToHost));
+    CHECK_CUDA(cudaMemcpy(&rs0, dRS, 4, cudaMemcpyDeviceToHost));
+    bool ok = rs0 == 0.5f / 127.f;
+    for (int8_t v : hY) ok = ok && v == 127;
+    if (!ok) {
+        std::printf("[SmoothQuant] known answer FAILED (expected y = 127, row_scale = 0.5/127)\n");
+        ++g_failures;
+    }
+    CHECK_CUDA(cudaFree(dX));
+    CHECK_CUDA(cudaFree(dY));
+    CHECK_CUDA(cudaFree(dS));
+    CHECK_CUDA(cudaFree(dRS));
+}
+
+static void test_moe_smoothquant(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t topk)
+{
+    std::mt19937 rng(42);
+    std::uniform_int_distribution<int> edist(0, (int)experts - 1);
+    std::vector<uint16_t> hX((size_t)tokens * hidden, half_of(0.5f));
+    std::vector<float> hS((size_t)experts * hidden, 1.f);
+    std::vector<int32_t> hIds((size_t)tokens * topk);
+    for (uint32_t t = 0; t < tokens; ++t) {  // distinct expert ids per token
+        std::set<int> used;
+        for (uint32_t k = 0; k < topk; ++k) {
+            int e = edist(rng);
+            while (used.count(e)) e = edist(rng);
+            used.insert(e);
+            hIds[(size_t)t * topk + k] = e;
+        }
+    }
+    const size_t rows = (size_t)tokens * topk;
+    void* dX;
+    float *dS, *dRS;
+    int32_t* dIds;
+    int8_t* dQ;
+    CHECK_CUDA(cudaMalloc(&dX, hX.size() * 2));
+    CHECK_CUDA(cudaMalloc(&dS, hS.size() * 4));
+    CHECK_CUDA(cudaMalloc(&dIds, hIds.size() * 4));
+    CHECK_CUDA(cudaMalloc(&dQ, rows * hidden));
+    CHECK_CUDA(cudaMalloc(&dRS, rows * 4));
+    CHECK_CUDA(cudaMemcpy(dX, hX.data(), hX.size() * 2, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dS, hS.data(), hS.size() * 4, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dIds, hIds.data(), hIds.size() * 4, cudaMemcpyHostToDevice));
+    auto fn = [&] {
+        CHECK_B2SQ(b2sq_moe_smoothquant(dX, dS, dIds, dQ, dRS, tokens, hidden, topk, experts, 127.f, nullptr, nullptr));
+    };
+    const double ms = bench(fn);
+    const double bw = ((double)tokens * hidden * 2 + (double)experts * hidden * 4 + (double)tokens * topk * 4 +
+                       (double)rows * hidden + (double)rows * 4) /
+                      (ms * 1e-3) / 1e9;
+    std::printf("[MoE-SmoothQuant] tokens=%u hidden=%u experts=%u topk=%u  %g ms  %g GB/s\n", tokens, hidden, experts,
+                topk, ms, bw);
+    std::vector<int8_t> hQ(rows * hidden);
+    CHECK_CUDA(cudaMemcpy(hQ.data(), dQ, hQ.size(), cudaMemcpyDeviceToHost));
+    bool ok = true;
+    for (int8_t v : hQ) ok = ok && v == 127;
+    if (!ok) {
+        std::printf("[MoE-SmoothQuant] known answer FAILED\n");
+        ++g_failures;
+    }
+    CHECK_CUDA(cudaFree(dX));
+    CHECK_CUDA(cudaFree(dS));
+    CHECK_CUDA(cudaFree(dIds));
+    CHECK_CUDA(cudaFree(dQ));
+    CHECK_CUDA(cudaFree(dRS));
+}
+
+// The reference's layouts (A column-major lda = m, B row-major ldb = n, C
+// row-major; rocwmma_gemm_quantized.cpp:92-94, :205) and tensor-scale mode
+// with scale_a = scale_b = 1/127 (:227), int8 in place of fp8.
+static void test_quant_gemm(uint32_t m, uint32_t n, uint32_t k)
+{
+    int8_t *dA, *dB;
+    uint16_t* dC;
+    CHECK_CUDA(cudaMalloc(&dA, (size_t)m * k));
+    CHECK_CUDA(cudaMalloc(&dB, (size_t)k * n));
+    CHECK_CUDA(cudaMalloc(&dC, (size_t)m * n * 2));
+    CHECK_CUDA(cudaMemset(dA, 1, (size_t)m * k));
+    CHECK_CUDA(cudaMemset(dB, 1, (size_t)k * n));
+    size_t ws_bytes = 0;
+    CHECK_B2SQ(b2sq_gemm_i8_workspace_size(m, n, k, B2SQ_COL_MAJOR, B2SQ_ROW_MAJOR, &ws_bytes));
+    void* ws = nullptr;
+    if (ws_bytes) {
+        CHECK_CUDA(cudaMalloc(&ws, ws_bytes));
+        CHECK_CUDA(cudaMemset(ws, 0, ws_bytes));
+    }
+    const float s = 1.f / 127.f;
+    auto fn = [&] {
+        CHECK_B2SQ(b2sq_gemm_i8(m, n, k, dA, B2SQ_COL_MAJOR, m, dB, B2SQ_ROW_MAJOR, n, dC, B2SQ_F16, n, nullptr,
+                                nullptr, s, s, ws, ws_bytes, nullptr));
+    };
+    const double ms = bench(fn);
+    const double tflops = 2.0 * m * n * k / (ms * 1e-3) / 1e12;
+    std::printf("[QuantGEMM-I8] M=%u N=%u K=%u  %g ms  %g TFlops/s\n", m, n, k, ms, tflops);
+    // Known answer: every accumulator is k; every output fp16(k * (s * s)).
+    std::vector<uint16_t> hC((size_t)m * n);
+    CHECK_CUDA(cudaMemcpy(hC.data(), dC, hC.size() * 2, cudaMemcpyDeviceToHost));
+    int32_t* dI;
+    CHECK_CUDA(cudaMalloc(&dI, (size_t)4 * n));
+    CHECK_B2SQ(b2sq_gemm_i8(1, n, k, dA, B2SQ_COL_MAJOR, m, dB, B2SQ_ROW_MAJOR, n, dI, B2SQ_I32, n, nullptr, nullptr,
+                            1.f, 1.f, nullptr, 0, nullptr));
+    std::vector<int32_t> hI(n);
+    CHECK_CUDA(cudaMemcpy(hI.data(), dI, (size_t)4 * n, cudaMemcpyDeviceToHost));
+    bool ok = true;
+    for (int32_t v : hI) ok = ok && v == (int32_t)k;
+    for (size_t i = 1; i < hC.size(); ++i) ok = ok && hC[i] == hC[0];
+    if (!ok) {
+        std::printf("[QuantGEMM-I8] known answer FAILED\n");
+        ++g_failures;
+    }
+    CHECK_CUDA(cudaFree(dI));
+    CHECK_CUDA(cudaFree(dA));
+    CHECK_CUDA(cudaFree(dB));
+    CHECK_CUDA(cudaFree(dC));
+    if (ws) CHECK_CUDA(cudaFree(ws));
+}
+
+static void test_moe_sorting(uint32_t tokens, uint32_t experts, uint32_t topk, uint32_t unit)
+{
+    std::mt19937 rng(42);
+    std::uniform_int_distribution<int> edist(0, (int)experts - 1);
+    std::vector<int32_t> hIds((size_t)tokens * topk);
+    for (auto& v : hIds) v = edist(rng);
+    int32_t *dIds, *dCnt, *dStart, *dSorted;
+    CHECK_CUDA(cudaMalloc(&dIds, hIds.size() * 4));
+    CHECK_CUDA(cudaMalloc(&dCnt, experts * 4));
+    CHECK_CUDA(cudaMalloc(&dStart, (experts + 1) * 4));
+    CHECK_CUDA(cudaMalloc(&dSorted, ((size_t)tokens * topk + (size_t)experts * unit) * 4));
+    CHECK_CUDA(cudaMemcpy(dIds, hIds.data(), hIds.size() * 4, cudaMemcpyHostToDevice));
+    auto fn = [&] {
+        CHECK_B2SQ(b2sq_moe_sorting(dIds, tokens, topk, experts, unit, dCnt, dStart, dSorted, nullptr, nullptr));
+    };
+    const double ms = bench(fn, 3, 10);
+    std::printf("[MoE-Sorting] tokens=%u experts=%u topk=%u unit=%u  %g ms\n", tokens, experts, topk, unit, ms);
+    std::vector<int32_t> hCnt(experts);
+    CHECK_CUDA(cudaMemcpy(hCnt.data(), dCnt, experts * 4, cudaMemcpyDeviceToHost));
+    uint64_t total = 0;
+    for (int32_t c : hCnt) total += (uint64_t)c;
+    if (total != hIds.size()) {
+        std::printf("[MoE-Sorting] known answer FAILED (counts do not sum to tokens*topk)\n");
+        ++g_failures;
+    }
+    CHECK_CUDA(cudaFree(dIds));
+    CHECK_CUDA(cudaFree(dCnt));
+    CHECK_CUDA(cudaFree(dStart));
+    CHECK_CUDA(cudaFree(dSorted));
+}
+
+int main(int argc, char** argv)
+{
+    cudaDeviceProp prop;
+    CHECK_CUDA(cudaGetDeviceProperties(&prop, 0));
+    std::printf("Device: %s  (%s)\n\n", prop.name, b2sq_version());
+    const std::string what = argc > 1 ? argv[1] : "all";
+    if (what == "smoothquant" || what == "all") {
+        uint32_t M = 3328, N = 4096;  // rocwmma_smoothquant.cpp:170-174
+        if (argc >= 4) M = (uint32_t)std::atoi(argv[2]), N = (uint32_t)std::atoi(argv[3]);
+        std::printf("=== SmoothQuant (b2sq, sm_100a) ===\n");
+        test_smoothquant(M, N);
+        for (uint32_t n : {1024u, 2048u, 8192u}) test_smoothquant(M, n);
+    }
+    if (what == "moe" || what == "all") {
+        std::printf("=== MoE SmoothQuant (b2sq, sm_100a) ===\n");  // rocwmma_moe_smoothquant.cpp:202-204
+        test_moe_smoothquant(3328, 4096, 32, 5);
+        test_moe_smoothquant(3328, 4096, 8, 2);
+        test_moe_smoothquant(3328, 8192, 64, 5);
+    }
+    if (what == "gemm" || what == "all") {
+        std::printf("=== Quantized GEMM, int8 (b2sq, sm_100a) ===\n");  // rocwmma_gemm_quantized.cpp:264-266
+        test_quant_gemm(3840, 4096, 4096);
+        test_quant_gemm(4096, 4096, 4096);
+        test_quant_gemm(8192, 8192, 8192);
+    }
+    if (what == "sorting" || what == "all") {
+        std::printf("=== MoE Sorting (b2sq, sm_100a) ===\n");
+        // rocwmma_moe_sorting.cpp:201-207
+        test_moe_sorting(3328, 8, 4, 32);
+        for (auto ek : {std::pair<uint32_t, uint32_t>{16, 2}, {32, 4}, {64, 5}, {128, 8}})
+            test_moe_sorting(3328, ek.first, ek.second, 32);
+    }
+    return g_failures ? 1 : 0;
+}
