@@ -562,60 +562,6 @@ __global__ void __launch_bounds__(kTmaThreads) sq_tma_kernel(const __half* __res
     if (threadIdx.x == 0) bulk_wait_all();
 }
 
-template <int VPT>
-__global__ void __launch_bounds__(kTmaThreads) moe_sq_tma_kernel(const __half* __restrict__ x,
-                                                                 const float* __restrict__ smooth,
-                                                                 const int32_t* __restrict__ topk_ids,
-                                                                 int8_t* __restrict__ qy,
-                                                                 float* __restrict__ row_scale, uint32_t tokens,
-                                                                 uint32_t hidden, uint32_t topk, uint32_t experts,
-                                                                 float qmax, const int32_t* __restrict__ row_perm,
-                                                                 uint32_t stages, uint32_t stage_bytes, uint32_t out_bytes)
-{
-    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
-    extern __shared__ __align__(128) uint8_t smem[];
-    const TmaRing r = tma_ring(smem, stages, stage_bytes);
-    const uint32_t out_base = r.data + stages * stage_bytes + kTmaReserved;
-    const uint32_t out_stride = (out_bytes + 127) & ~127u;
-    tma_ring_init(r, stages);
-    const uint32_t nvec = hidden / 8;
-    if (threadIdx.x >= kTmaConsumers) {
-        if (threadIdx.x == kTmaConsumers) tma_produce(r, x, tokens, hidden, stages, stage_bytes);
-        return;
-    }
-    uint32_t i = 0, parity = 0;
-    for (uint64_t tok = blockIdx.x; tok < tokens; tok += gridDim.x, ++i) {
-        uint4 raw[VPT];
-        if (!tma_consume<VPT>(r, i, stages, stage_bytes, nvec, raw)) break;
-#pragma unroll 1
-        for (uint32_t k = 0; k < topk; ++k, parity ^= 1) {
-            const uint64_t flat = tok * topk + k;
-            const int32_t eid = __ldg(topk_ids + flat);
-            const int64_t rr = row_perm ? (int64_t)__ldg(row_perm + flat) : (int64_t)flat;
-            const bool ok = eid >= 0 && (uint32_t)eid < experts && rr >= 0;  // reference :86-87
-            const float* srow = smooth + (size_t)(ok ? eid : 0) * hidden;
-            float xs[VPT][8];
-#pragma unroll
-            for (int j = 0; j < VPT; ++j) {
-                const uint32_t v = j * kTmaConsumers + threadIdx.x;
-                float xf[8];
-                unpack8(raw[j], xf);
-                if (ok && v < nvec) {
-                    scale8(xf, srow + (size_t)v * 8, xs[j]);
-                } else {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) xs[j][q] = 0.f;
-                }
-            }
-            bool fast;
-            const float amax = row_absmax<VPT>(xs, r.red, parity, qmax, &fast);
-            tma_quantize_out<VPT>(xs, amax, fast, qy + (size_t)rr * hidden, row_scale + rr, nvec, qmax, ok,
-                                  out_base + parity * out_stride, out_bytes);
-        }
-    }
-    if (threadIdx.x == 0) bulk_wait_all();
-}
-
 // Generic fallback: one block per output row, two passes over the row (the
 // reference's own structure), any N and any alignment.  Used for N % 8 != 0,
 // unaligned pointers and rows longer than the register-resident limit.
@@ -751,7 +697,9 @@ unsigned generic_grid(uint64_t rows)
 namespace {
 
 // Inputs of at least this many elements take the streaming kernels.
-constexpr uint64_t kTmaMinElems = 1ull << 22;
+// (crossover measured on B200: at 3328 x 4096 the register-resident kernel is
+// faster, from 3328 x 8192 up the streaming one)
+constexpr uint64_t kTmaMinElems = 1ull << 24;
 constexpr uint32_t kTmaRingBytes = 110 * 1024;  // input ring per CTA: two CTAs per SM for 16 KiB rows
 
 struct TmaCfg {
@@ -796,19 +744,6 @@ cudaError_t launch_sq_tma(const __half* x, const float* s, int8_t* y, float* rs,
     if (e != cudaSuccess) return e;
     sq_tma_kernel<VPT><<<grid, kTmaThreads, c.smem, st>>>(x, s, y, rs, M, N, qmax, c.stages, c.stage_bytes,
                                                           c.out_bytes);
-    return cudaGetLastError();
-}
-
-template <int VPT>
-cudaError_t launch_moe_tma(const __half* x, const float* s, const int32_t* ids, int8_t* qy, float* rs, uint32_t T,
-                           uint32_t H, uint32_t K, uint32_t E, float qmax, const int32_t* perm, cudaStream_t st)
-{
-    const TmaCfg c = tma_cfg(H, qy);
-    unsigned grid = 0;
-    cudaError_t e = persistent_grid(moe_sq_tma_kernel<VPT>, c.smem, T, &grid);
-    if (e != cudaSuccess) return e;
-    moe_sq_tma_kernel<VPT><<<grid, kTmaThreads, c.smem, st>>>(x, s, ids, qy, rs, T, H, K, E, qmax, perm, c.stages,
-                                                              c.stage_bytes, c.out_bytes);
     return cudaGetLastError();
 }
 
@@ -880,11 +815,9 @@ cudaError_t launch_moe_smoothquant(const void* x, const float* s, const int32_t*
                                                                                   qmax, perm);
         return cudaGetLastError();
     }
-    uint32_t vpt = 0;
-    if (use_tma(T, H, vpt)) {
-        if (used_vector_path) *used_vector_path = 2;
-        B2SQ_TMA_DISPATCH(launch_moe_tma, vpt, xh, s, ids, qy, rs, T, H, K, E, qmax, perm, st)
-    }
+    // MoE uses the register-resident row groups at every size: a streaming
+    // (TMA-staged) variant measured slower at every configuration tried (its
+    // per-slot reductions are latency-bound; many tokens in flight win).
     B2SQ_VEC_DISPATCH(launch_moe, xh, s, ids, qy, rs, T, H, K, E, qmax, perm, st)
 }
 

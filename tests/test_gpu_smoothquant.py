@@ -128,11 +128,11 @@ def test_special_values_and_qmax(cuda_device, qmax):
 
 @pytest.mark.parametrize("qmax", [127.0, 100.5])
 def test_special_values_streaming_path(cuda_device, qmax):
-    """Inputs of >= 4M elements take the TMA-staged kernel; rows with NaN, +-inf,
+    """Inputs of >= 16M elements take the TMA-staged kernel; rows with NaN, +-inf,
     overflow to inf after smoothing, or all-subnormal values take its exact
     (clamped) branch, ordinary rows its fast branch.  All bit-exact."""
     rng = np.random.default_rng(77)
-    M, N = 4096, 1024
+    M, N = 17000, 1024  # >= 2^24 elements, also with N = 1000
     x = synth.activations_np(rng, M, N, 8, 20.0)
     s = synth.smooth_np(rng, N)
     x[10, 5] = np.nan
