@@ -213,6 +213,27 @@ B2SQ_API b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k,
 /* ------------------------------------------------------------------------ */
 
 /*
+ * MoE router, replacing kernel_topk_softmax / kernel_topk_softmax_large
+ * (rocwmma_topk_softmax.cpp:58-131, :137-187; launch :222-231).  For fp16
+ * logits [tokens, experts] (row-major, ld = experts):
+ *   topk_weights[t, k]  softmax probability of the k-th choice (fp32)
+ *   topk_indices[t, k]  its expert id (int32)
+ * Same selection rules as the reference: equal probabilities resolve in the
+ * order of its wave64 shfl_down arg-max tree (lane l takes lane l + off only
+ * when strictly greater: the first pick is the lowest id, later picks follow
+ * the tree, e.g. 0, 4, 2 for eight equal logits); for experts <= 64, min(topk, experts) slots are written (the rest are left
+ * untouched); for experts > 64 only experts 0..63 are candidates and all topk
+ * slots are written, (-1.0f, -1) once no candidate is left.  The exp-sum is
+ * accumulated in the reference's wave64 order; exp() itself is the library's
+ * own fp32 evaluation (within 1 ulp), so probabilities match any platform
+ * expf to a few ulp.  topk_indices may feed b2sq_moe_sorting directly.
+ */
+B2SQ_API b2sq_status b2sq_topk_softmax(const void* logits_f16, float* topk_weights,
+                                       int32_t* topk_indices, uint32_t tokens,
+                                       uint32_t experts, uint32_t topk,
+                                       b2sq_stream_t stream);
+
+/*
  * Replaces the histogram / padded prefix / scatter kernels of
  * rocwmma_moe_sorting.cpp (:53-77, :82-101, :107-125).  For topk_ids
  * [tokens, topk]:

@@ -20,6 +20,8 @@ from .api import (  # noqa: F401
     plan,
     smoothquant,
     smoothquant_gemm,
+    topk_softmax,
+    kernel_topk_softmax,
     workspace_size,
 )
 

@@ -10,6 +10,8 @@ this module                reference operator (file:line)
 ``moe_smoothquant``        kernel_moe_smoothquant, rocwmma_moe_smoothquant.cpp:69-76
 ``gemm_quant``             gemm_quant_tensor_scale, rocwmma_gemm_quantized.cpp:127-132
                            (+ the per-row x per-column mode of its header, :20/:26)
+``topk_softmax``           kernel_topk_softmax(_large), rocwmma_topk_softmax.cpp:58-64, :137-141
+``moe_sorting``            kernel_moe_sorting_*, rocwmma_moe_sorting.cpp:53-125
 =========================  ===================================================
 
 Errors: the reference exits on a HIP error (CHECK_HIP, common.hpp:33-46) and
@@ -224,6 +226,33 @@ gemm_quant_tensor_scale = gemm_quant
 
 
 # ----------------------------------------------------------------------------- MoE
+def topk_softmax(logits: torch.Tensor, topk: int, topk_weights: Optional[torch.Tensor] = None,
+                 topk_indices: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None):
+    """MoE router (rocwmma_topk_softmax.cpp): softmax over fp16 logits
+    [tokens, experts], then the top-k experts per token.
+
+    Returns (topk_weights fp32 [tokens, topk], topk_indices int32 [tokens, topk]).
+    With experts <= 64 and topk > experts the slots past `experts` are left as
+    they were (zeros when the outputs are allocated here)."""
+    if logits.dtype != torch.float16 or logits.dim() != 2 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous fp16 [tokens, experts] tensor")
+    T, E = logits.shape
+    dev = _need_cuda(logits, topk_weights, topk_indices)
+    if topk_weights is None:
+        topk_weights = torch.zeros((T, topk), dtype=torch.float32, device=dev)
+    if topk_indices is None:
+        topk_indices = torch.zeros((T, topk), dtype=torch.int32, device=dev)
+    if (topk_weights.shape != (T, topk) or topk_indices.shape != (T, topk) or topk_weights.dtype != torch.float32
+            or topk_indices.dtype != torch.int32 or not topk_weights.is_contiguous()
+            or not topk_indices.is_contiguous()):
+        raise ValueError("topk_weights / topk_indices must be contiguous fp32 / int32 [tokens, topk]")
+    lib = _lib.load()
+    st = lib.b2sq_topk_softmax(logits.data_ptr(), topk_weights.data_ptr(), topk_indices.data_ptr(), T, E, topk,
+                               _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_topk_softmax")
+    return topk_weights, topk_indices
+
+
 def moe_sorting(topk_ids: torch.Tensor, experts: int, unit_size: int = 1,
                 stream: Optional[torch.cuda.Stream] = None):
     """Groups (token, slot) pairs by expert (rocwmma_moe_sorting.cpp).
@@ -299,3 +328,6 @@ def smoothquant_gemm(x: torch.Tensor, smooth_scale: torch.Tensor, w_nk: torch.Te
                                       _stream_ptr(stream, dev))
     _lib.check(st, "b2sq_smoothquant_gemm_i8")
     return c, xq, row_scale
+
+
+kernel_topk_softmax = topk_softmax

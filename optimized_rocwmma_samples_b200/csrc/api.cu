@@ -325,6 +325,23 @@ b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* smooth_scal
                         scale_w, workspace, workspace_bytes, stream, true);
 }
 
+b2sq_status b2sq_topk_softmax(const void* logits_f16, float* topk_weights, int32_t* topk_indices, uint32_t tokens,
+                              uint32_t experts, uint32_t topk, b2sq_stream_t stream)
+{
+    if (tokens == 0 || experts == 0 || topk == 0) return ok();  // the reference writes nothing
+    if ((uint64_t)tokens * experts > 0x7fffffffffffull || (uint64_t)tokens * topk > 0x7fffffffffffull)
+        return fail(B2SQ_ERR_INVALID_ARG, "topk_softmax: tokens * experts too large");
+    if ((uint64_t)tokens * (experts > 64 ? 32 : 8) / 128 >= 0x7fffffffull)
+        return fail(B2SQ_ERR_INVALID_ARG, "topk_softmax: too many tokens for one launch");
+    if (!logits_f16 || !topk_weights || !topk_indices) return fail(B2SQ_ERR_INVALID_ARG, "topk_softmax: null pointer");
+    if (!aligned(logits_f16, 2) || !aligned(topk_weights, 4) || !aligned(topk_indices, 4))
+        return fail(B2SQ_ERR_INVALID_ARG, "topk_softmax: misaligned pointer");
+    cudaError_t e = b2sq::launch_topk_softmax(logits_f16, topk_weights, topk_indices, tokens, experts, topk,
+                                              reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "topk_softmax launch");
+    return ok();
+}
+
 b2sq_status b2sq_moe_sorting(const int32_t* topk_ids, uint32_t tokens, uint32_t topk, uint32_t experts,
                              uint32_t unit_size, int32_t* expert_count, int32_t* expert_start,
                              int32_t* sorted_token_ids, int32_t* row_perm, b2sq_stream_t stream)

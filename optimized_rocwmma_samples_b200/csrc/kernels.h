@@ -98,6 +98,10 @@ cudaError_t launch_moe_sort(const int32_t* ids, uint32_t tokens, uint32_t topk, 
                             int32_t* expert_count, int32_t* expert_start, int32_t* sorted_ids, int32_t* row_perm,
                             cudaStream_t st);
 
+// MoE router: softmax over expert logits + top-k (moe_route.cu).
+cudaError_t launch_topk_softmax(const void* logits, float* topk_w, int32_t* topk_i, uint32_t tokens,
+                                uint32_t experts, uint32_t topk, cudaStream_t st);
+
 // Debug: a kernel that waits for an mbarrier nobody arrives on, with a limit.
 cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st);
 

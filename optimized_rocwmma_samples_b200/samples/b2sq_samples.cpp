@@ -5,6 +5,7 @@
 //   rocwmma_moe_smoothquant.cpp:147-206  [MoE-SmoothQuant] tokens=.. ...  X ms  Y GB/s
 //   rocwmma_gemm_quantized.cpp:197-268   [QuantGEMM-I8] M=.. N=.. K=..  X ms  Y TFlops/s
 //   rocwmma_moe_sorting.cpp:141-208      [MoE-Sorting] tokens=.. experts=.. topk=.. unit=..  X ms
+//   rocwmma_topk_softmax.cpp:197-256     [TopK-Softmax] tokens=.. experts=.. topk=..  X ms  Y GB/s
 //
 // so output parsers written for the reference (benchmark.sh:177-188) read it
 // unchanged.  Inputs are the reference drivers' constants (x = 0.5, smooth = 1,
@@ -13,7 +14,7 @@
 // sample also checks the known answer its constant inputs imply and exits
 // non-zero on a mismatch (the reference checks nothing here).
 //
-//   b2sq_samples [smoothquant|moe|gemm|sorting|all] [M N]
+//   b2sq_samples [smoothquant|moe|gemm|sorting|topk|all] [M N]
 #include "../../include/b2sq.h"
 
 #include <cuda_runtime.h>
@@ -239,6 +240,68 @@ static void test_moe_sorting(uint32_t tokens, uint32_t experts, uint32_t topk, u
     CHECK_CUDA(cudaFree(dSorted));
 }
 
+// rocwmma_topk_softmax.cpp:197-240: logits = rand()/RAND_MAX - 0.5 in fp16, GB/s
+// over logits read + weights and indices written.  Known answer: in every row
+// the indices are distinct expert ids and the weights never increase (each
+// pick is the largest remaining probability).
+static void test_topk_softmax(uint32_t tokens, uint32_t experts, uint32_t topk)
+{
+    std::mt19937 rng(7);
+    std::uniform_real_distribution<float> u(-0.5f, 0.5f);
+    std::vector<uint16_t> hL((size_t)tokens * experts);
+    for (auto& v : hL) {
+        const float f = u(rng);  // round to fp16 through its bit pattern (|f| < 1, normal or zero)
+        uint32_t b;
+        std::memcpy(&b, &f, 4);
+        const uint32_t sign = (b >> 16) & 0x8000u;
+        const int ex = (int)((b >> 23) & 0xff) - 127 + 15;
+        uint32_t man = b & 0x7fffffu;
+        if (ex <= 0) {
+            v = (uint16_t)sign;  // tiny values flush to a signed zero here; fine for a routing input
+        } else {
+            uint32_t h = ((uint32_t)ex << 10) | (man >> 13);
+            const uint32_t rem = man & 0x1fffu;
+            if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+            v = (uint16_t)(sign | h);
+        }
+    }
+    void* dL;
+    float* dW;
+    int32_t* dI;
+    CHECK_CUDA(cudaMalloc(&dL, hL.size() * 2));
+    CHECK_CUDA(cudaMalloc(&dW, (size_t)tokens * topk * 4));
+    CHECK_CUDA(cudaMalloc(&dI, (size_t)tokens * topk * 4));
+    CHECK_CUDA(cudaMemcpy(dL, hL.data(), hL.size() * 2, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemset(dW, 0, (size_t)tokens * topk * 4));
+    CHECK_CUDA(cudaMemset(dI, 0, (size_t)tokens * topk * 4));
+    auto fn = [&] { CHECK_B2SQ(b2sq_topk_softmax(dL, dW, dI, tokens, experts, topk, nullptr)); };
+    const double ms = bench(fn);
+    const double gbs = ((double)tokens * experts * 2 + (double)tokens * topk * 8) / (ms * 1e-3) / 1e9;
+    std::printf("[TopK-Softmax] tokens=%u experts=%u topk=%u  %g ms  %g GB/s\n", tokens, experts, topk, ms, gbs);
+    std::vector<float> hW((size_t)tokens * topk);
+    std::vector<int32_t> hI((size_t)tokens * topk);
+    CHECK_CUDA(cudaMemcpy(hW.data(), dW, hW.size() * 4, cudaMemcpyDeviceToHost));
+    CHECK_CUDA(cudaMemcpy(hI.data(), dI, hI.size() * 4, cudaMemcpyDeviceToHost));
+    const uint32_t picks = topk < experts ? topk : experts;
+    bool good = true;
+    for (uint32_t t = 0; t < tokens && good; ++t) {
+        std::set<int32_t> seen;
+        for (uint32_t k = 0; k < picks; ++k) {
+            const int32_t id = hI[(size_t)t * topk + k];
+            const float w = hW[(size_t)t * topk + k];
+            if (id < 0 || (uint32_t)id >= experts || !seen.insert(id).second || !(w > 0.f && w <= 1.f)) good = false;
+            if (k && w > hW[(size_t)t * topk + k - 1]) good = false;
+        }
+    }
+    if (!good) {
+        std::printf("[TopK-Softmax] known answer FAILED\n");
+        ++g_failures;
+    }
+    CHECK_CUDA(cudaFree(dL));
+    CHECK_CUDA(cudaFree(dW));
+    CHECK_CUDA(cudaFree(dI));
+}
+
 int main(int argc, char** argv)
 {
     cudaDeviceProp prop;
@@ -270,6 +333,13 @@ int main(int argc, char** argv)
         test_moe_sorting(3328, 8, 4, 32);
         for (auto ek : {std::pair<uint32_t, uint32_t>{16, 2}, {32, 4}, {64, 5}, {128, 8}})
             test_moe_sorting(3328, ek.first, ek.second, 32);
+    }
+    if (what == "topk" || what == "all") {
+        std::printf("=== TopK-Softmax (b2sq, sm_100a) ===\n");
+        // rocwmma_topk_softmax.cpp:247-255
+        test_topk_softmax(128, 8, 4);
+        for (auto ek : {std::pair<uint32_t, uint32_t>{8, 2}, {16, 2}, {32, 5}, {64, 5}})
+            test_topk_softmax(3328, ek.first, ek.second);
     }
     return g_failures ? 1 : 0;
 }

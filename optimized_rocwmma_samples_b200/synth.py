@@ -61,8 +61,8 @@ def scales_np(rng, n: int) -> np.ndarray:
 
 
 def topk_routing_np(rng, tokens: int, experts: int, topk: int) -> np.ndarray:
-    """softmax(N(0,1) logits) -> top-k expert ids, ties to the lower id
-    (the selection rule of rocwmma_topk_softmax.cpp:115-118)."""
+    """softmax(N(0,1) logits) -> top-k expert ids.  Continuous logits have no
+    ties; the device router (b2sq_topk_softmax) is the exact counterpart."""
     logits = rng.standard_normal((tokens, experts), dtype=np.float32)
     z = np.exp(logits - logits.max(axis=1, keepdims=True))
     p = z / z.sum(axis=1, keepdims=True)

@@ -47,6 +47,9 @@ def load() -> C.CDLL:
         lib.oracle_float_to_bf16.argtypes = [f32]
         lib.oracle_float_to_bf16.restype = C.c_uint16
         lib.oracle_num_threads.restype = i
+        lib.oracle_topk_softmax.argtypes = [vp, vp, vp, u32, u32, u32]
+        lib.oracle_route_exp.argtypes = [f32]
+        lib.oracle_route_exp.restype = f32
         _lib = lib
     return _lib
 
@@ -126,6 +129,23 @@ def gemm_quant(a, b, sa_row=None, sb_col=None, scale_a=1.0, scale_b=1.0, out_dty
     """(acc int32, out uint16 bits) of the full reference-style quantized GEMM."""
     acc = gemm_i8_acc(a, b)
     return acc, dequant(acc, sa_row, sb_col, scale_a, scale_b, out_dtype)
+
+
+def topk_softmax(logits: np.ndarray, topk: int, out_w=None, out_i=None):
+    """rocwmma_topk_softmax.cpp:58-187 restated (oracle.c: oracle_topk_softmax).
+    logits fp16 [tokens, experts]; returns (weights fp32, indices int32), each
+    [tokens, topk], starting from out_w / out_i (zeros) for unwritten slots."""
+    x = np.ascontiguousarray(logits, dtype=np.float16)
+    T, E = x.shape
+    w = np.zeros((T, topk), np.float32) if out_w is None else out_w.copy()
+    i = np.zeros((T, topk), np.int32) if out_i is None else out_i.copy()
+    if T and E and topk:
+        load().oracle_topk_softmax(_p(x), _p(w), _p(i), T, E, topk)
+    return w, i
+
+
+def route_exp(a: float) -> float:
+    return load().oracle_route_exp(a)
 
 
 def moe_sorting(topk_ids, experts: int, unit_size: int = 1):

@@ -192,3 +192,62 @@ def test_kat_moe_sorting():
     assert list(start) == [0, 4, 8, 12]  # counts padded to 4 (:93-96), sentinel total at [E]
     assert list(sids[:12]) == [0, 3, 4, 4, 1, 4, 4, 4, 0, 1, 2, 4]  # padding slots hold `tokens` (4)
     assert list(perm) == [0, 8, 9, 4, -1, 10, 1, -1]
+
+
+# ----------------------------------------------------------------- MoE router
+def np_topk_softmax(logits16, topk):
+    """Independent restatement for well-separated inputs: float64 softmax, stable
+    arg-sort (ties to the lower id), as rocwmma_topk_softmax.cpp:58-131 selects."""
+    x = logits16.astype(np.float64)
+    z = np.exp(x - x.max(axis=1, keepdims=True))
+    p = z / z.sum(axis=1, keepdims=True)
+    order = np.argsort(-p, axis=1, kind="stable")[:, :topk]
+    return np.take_along_axis(p, order, axis=1), order.astype(np.int32)
+
+
+def test_route_exp_accuracy():
+    import math
+
+    rng = np.random.default_rng(5)
+    xs = np.concatenate([rng.uniform(-103.9, 88.7, 20000), rng.uniform(-1, 0, 5000)]).astype(np.float32)
+    for x in xs:
+        t = math.exp(float(x))
+        ulp = float(np.spacing(np.float32(t))) if t >= float(np.finfo(np.float32).tiny) else 2.0 ** -149
+        assert abs(O.route_exp(float(x)) - t) <= ulp, x
+    assert O.route_exp(0.0) == 1.0 and O.route_exp(float("-inf")) == 0.0 and O.route_exp(-200.0) == 0.0
+    assert O.route_exp(100.0) == float("inf") and math.isnan(O.route_exp(float("nan")))
+
+
+@pytest.mark.parametrize("E,K", [(8, 2), (16, 2), (32, 5), (64, 5), (5, 3), (128, 4), (300, 8)])
+def test_topk_softmax_matches_float64_restatement(E, K):
+    rng = np.random.default_rng(E * 10 + K)
+    T = 256
+    # distinct logits per row (a permutation of a spread grid): no near-ties
+    grid = np.linspace(-4, 4, E).astype(np.float16)
+    logits = np.stack([rng.permutation(grid) for _ in range(T)])
+    w, i = O.topk_softmax(logits, K)
+    w64, i64 = np_topk_softmax(logits, K)
+    if E > 64:  # the wide variant only considers experts 0..63 (rocwmma_topk_softmax.cpp:160-164)
+        w64, i64 = np_topk_softmax(logits[:, :64], K)
+        full = np.exp(logits.astype(np.float64) - logits.astype(np.float64).max(1, keepdims=True))
+        w64 = w64 * full[:, :64].sum(1, keepdims=True) / full.sum(1, keepdims=True)
+    assert np.array_equal(i, i64)
+    assert np.allclose(w, w64, rtol=4e-7, atol=0)
+
+
+def test_topk_softmax_ties_and_edges():
+    # equal logits: equal probabilities; ties resolve in the wave's shfl_down
+    # tree order (lane l takes lane l+off only if strictly greater), which after
+    # lane 0 is masked reaches lane 4 through offset 4 first: 0, then 4, then 2
+    w, i = O.topk_softmax(np.zeros((2, 8), np.float16), 3)
+    assert i.tolist() == [[0, 4, 2]] * 2 and np.all(w == np.float32(0.125))
+    # topk > experts (<= 64): slots past `experts` untouched
+    w, i = O.topk_softmax(np.array([[1.0, 3.0, 2.0]], np.float16), 5, out_w=np.full((1, 5), 7, np.float32),
+                          out_i=np.full((1, 5), 9, np.int32))
+    assert i.tolist() == [[1, 2, 0, 9, 9]] and w[0, 3] == 7
+    # wide variant exhausted: (-1, -1)
+    w, i = O.topk_softmax(np.zeros((1, 65), np.float16), 66)
+    assert i[0, 64] == -1 and w[0, 65] == -1 and sorted(i[0, :64].tolist()) == list(range(64))
+    # all -inf: NaN probabilities; the first lane keeps its NaN (other > NaN is false)
+    w, i = O.topk_softmax(np.full((1, 4), -np.inf, np.float16), 2)
+    assert np.isnan(w[0, 0]) and i[0, 0] == 0
