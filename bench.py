@@ -40,9 +40,9 @@ M = N = K = 8192
 FLUSH_BYTES = 512 << 20
 SQ_M, SQ_K = 16384, 8192
 
-# DRAM bytes (read + write) of one gemm_i8_kernel<256> launch at 8192^3, from
-# the ncu capture summarised in profiles/gemm_i8_8192_ncu.md.
-GEMM_TRAFFIC_BYTES = 444_898_048  # 333,052,672 read + 111,845,376 written
+# DRAM bytes (read + write) of one gemm_i8_pair_kernel launch at 8192^3, from
+# the ncu capture summarised in profiles/gemm_i8_pair_8192_ncu.md.
+GEMM_TRAFFIC_BYTES = 339_078_656  # 224,149,760 read + 114,928,896 written
 
 
 def parse():
