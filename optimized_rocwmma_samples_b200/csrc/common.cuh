@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "libb2sq is built for sm_100a only"
 #endif
@@ -216,6 +218,32 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Lets a kernel launched after this one with PDL start its prologue now.
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: launches a kernel that may start while the previous kernel of the
+// stream drains (programmatic stream serialization).  Every kernel launched
+// this way calls griddep_wait() before its first global-memory access, so it
+// observes everything the previous kernel wrote, whatever that kernel was,
+// and only then griddep_launch_dependents(), so a kernel chained after it
+// cannot start before the kernel before it has completed (the fused
+// smoothquant -> GEMM entry prefetches weights ahead of its own wait).  What
+// overlaps is the launch and the CTAs' start-up, which otherwise leave the
+// GPU idle for a couple of microseconds between two short kernels.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // CTA pairs (thread-block clusters of 2) for cta_group::2 MMAs.

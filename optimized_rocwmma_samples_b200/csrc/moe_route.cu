@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(kRouteThreads) topk_softmax_kernel(const __hal
                                                                      int32_t* __restrict__ topk_i, uint32_t tokens,
                                                                      uint32_t experts, uint32_t topk)
 {
+    griddep_wait();  // logits may come from the previous kernel (PDL launch)
+    griddep_launch_dependents();
     constexpr int V = P < 8 ? P : 8;  // virtual lanes per thread
     constexpr int G = P / V;          // threads per token
     const uint64_t gtid = (uint64_t)blockIdx.x * kRouteThreads + threadIdx.x;
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(kRouteThreads) topk_softmax_wide_kernel(const 
                                                                           uint32_t tokens, uint32_t experts,
                                                                           uint32_t topk)
 {
+    griddep_wait();
+    griddep_launch_dependents();
     const uint64_t tok = ((uint64_t)blockIdx.x * kRouteThreads + threadIdx.x) >> 5;
     const uint32_t t = threadIdx.x & 31;
     if (tok >= tokens) return;
@@ -255,8 +259,7 @@ cudaError_t launch_small(const __half* x, float* w, int32_t* idx, uint32_t token
     constexpr int G = P / (P < 8 ? P : 8);
     const uint64_t threads = (uint64_t)tokens * G;
     const unsigned grid = (unsigned)((threads + kRouteThreads - 1) / kRouteThreads);
-    topk_softmax_kernel<P><<<grid, kRouteThreads, 0, st>>>(x, w, idx, tokens, experts, topk);
-    return cudaGetLastError();
+    return launch_pdl(topk_softmax_kernel<P>, dim3(grid), dim3(kRouteThreads), 0, st, x, w, idx, tokens, experts, topk);
 }
 
 }  // namespace
@@ -267,8 +270,8 @@ cudaError_t launch_topk_softmax(const void* logits, float* topk_w, int32_t* topk
     const __half* x = static_cast<const __half*>(logits);
     if (experts > 64) {
         const unsigned grid = (unsigned)(((uint64_t)tokens * 32 + kRouteThreads - 1) / kRouteThreads);
-        topk_softmax_wide_kernel<<<grid, kRouteThreads, 0, st>>>(x, topk_w, topk_i, tokens, experts, topk);
-        return cudaGetLastError();
+        return launch_pdl(topk_softmax_wide_kernel, dim3(grid), dim3(kRouteThreads), 0, st, x, topk_w, topk_i, tokens,
+                          experts, topk);
     }
     if (experts <= 1) return launch_small<1>(x, topk_w, topk_i, tokens, experts, topk, st);
     if (experts <= 2) return launch_small<2>(x, topk_w, topk_i, tokens, experts, topk, st);

@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(kSortThreads) moe_sort_kernel(const int32_t* _
                                                                 int32_t* __restrict__ sorted_ids,
                                                                 int32_t* __restrict__ row_perm)
 {
+    griddep_wait();  // topk ids may come from the previous kernel (PDL launch)
+    griddep_launch_dependents();
     extern __shared__ int32_t sh[];
     int32_t* count = sh;                      // [E]
     int32_t* base = count + experts;          // [E] next free position per expert
@@ -112,9 +114,8 @@ cudaError_t launch_moe_sort(const int32_t* ids, uint32_t tokens, uint32_t topk, 
     const size_t smem = moe_sort_smem(experts);
     cudaError_t e = cudaFuncSetAttribute(moe_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    moe_sort_kernel<<<1, kSortThreads, smem, st>>>(ids, tokens, topk, experts, unit_size, expert_count,
-                                                   expert_start, sorted_ids, row_perm);
-    return cudaGetLastError();
+    return launch_pdl(moe_sort_kernel, dim3(1), dim3(kSortThreads), smem, st, ids, tokens, topk, experts, unit_size,
+                      expert_count, expert_start, sorted_ids, row_perm);
 }
 
 }  // namespace b2sq

@@ -219,7 +219,8 @@ __global__ void __launch_bounds__(kThreads) sq_vec_kernel(const __half* __restri
                                                           int8_t* __restrict__ y, float* __restrict__ row_scale,
                                                           uint32_t M, uint32_t N, float qmax)
 {
-    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
+    griddep_wait();               // the previous kernel's writes are visible from here on
+    griddep_launch_dependents();  // then a PDL-launched consumer may start its prologue
     __shared__ float red[kThreads / 32];
     constexpr int R = kThreads / G;
     const int lane_in_group = threadIdx.x % G;
@@ -265,7 +266,8 @@ __global__ void __launch_bounds__(kThreads) moe_sq_vec_kernel(const __half* __re
                                                               uint32_t experts, float qmax,
                                                               const int32_t* __restrict__ row_perm)
 {
-    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
+    griddep_wait();               // the previous kernel's writes are visible from here on
+    griddep_launch_dependents();  // then a PDL-launched consumer may start its prologue
     __shared__ float red[2][kThreads / 32];
     constexpr int R = kThreads / G;
     const int lane_in_group = threadIdx.x % G;
@@ -518,7 +520,8 @@ __global__ void __launch_bounds__(kTmaThreads) sq_tma_kernel(const __half* __res
                                                              uint32_t M, uint32_t N, float qmax, uint32_t stages,
                                                              uint32_t stage_bytes, uint32_t out_bytes)
 {
-    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
+    griddep_wait();               // the previous kernel's writes are visible from here on
+    griddep_launch_dependents();  // then a PDL-launched consumer may start its prologue
     extern __shared__ __align__(128) uint8_t smem[];
     const TmaRing r = tma_ring(smem, stages, stage_bytes);
     const uint32_t out_base = r.data + stages * stage_bytes + kTmaReserved;
@@ -596,7 +599,8 @@ __global__ void __launch_bounds__(kThreads) sq_generic_kernel(const __half* __re
                                                               int8_t* __restrict__ y, float* __restrict__ row_scale,
                                                               uint32_t M, uint32_t N, float qmax)
 {
-    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
+    griddep_wait();               // the previous kernel's writes are visible from here on
+    griddep_launch_dependents();  // then a PDL-launched consumer may start its prologue
     __shared__ float red[kThreads / 32];
     for (uint64_t row = blockIdx.x; row < M; row += gridDim.x)
         sq_row_generic(x + row * N, smooth, y + row * N, row_scale + row, N, qmax, red);
@@ -610,7 +614,8 @@ __global__ void __launch_bounds__(kThreads) moe_sq_generic_kernel(const __half* 
                                                                   uint32_t hidden, uint32_t topk, uint32_t experts,
                                                                   float qmax, const int32_t* __restrict__ row_perm)
 {
-    griddep_launch_dependents();  // a PDL-launched consumer may start its prologue
+    griddep_wait();               // the previous kernel's writes are visible from here on
+    griddep_launch_dependents();  // then a PDL-launched consumer may start its prologue
     __shared__ float red[kThreads / 32];
     const uint64_t total = (uint64_t)tokens * topk;
     for (uint64_t flat = blockIdx.x; flat < total; flat += gridDim.x) {
@@ -632,18 +637,19 @@ struct VecCfg {
     int VPT;
 };
 
-// Smallest register-resident configuration holding nvec 16-byte vectors per row.
+// Register-resident configuration for rows of nvec 16-byte vectors: the
+// smallest group G (a power of two in [32, 256]) that covers the row with at
+// most 4 vectors per thread, more only when G = 256 is not enough.  Four
+// 16-byte loads in flight per thread measured best on B200 at the
+// reference's sizes (3328 rows of 1024..4096, MoE 3328 x 4096): fewer
+// threads per row, fewer CTAs and waves, and no block barrier below G = 64.
 bool pick_cfg(uint32_t nvec, VecCfg& cfg)
 {
-    if (nvec <= 256) {
-        int g = 32;
-        while ((uint32_t)g < nvec) g <<= 1;
-        cfg = {g, 1};
-        return true;
-    }
-    const uint32_t vpt = (nvec + 255) / 256;
+    uint32_t g = 32;
+    while (g < 256 && g * 4 < nvec) g <<= 1;
+    const uint32_t vpt = (nvec + g - 1) / g;
     if (vpt > 8) return false;
-    cfg = {256, (int)vpt};
+    cfg = {(int)g, (int)(vpt ? vpt : 1)};
     return true;
 }
 
@@ -653,8 +659,7 @@ cudaError_t launch_sq(const __half* x, const float* s, int8_t* y, float* rs, uin
 {
     constexpr int R = kThreads / G;
     const uint64_t blocks = ((uint64_t)M + R - 1) / R;
-    sq_vec_kernel<G, VPT><<<(unsigned)blocks, kThreads, 0, st>>>(x, s, y, rs, M, N, qmax);
-    return cudaGetLastError();
+    return launch_pdl(sq_vec_kernel<G, VPT>, dim3((unsigned)blocks), dim3(kThreads), 0, st, x, s, y, rs, M, N, qmax);
 }
 
 template <int G, int VPT>
@@ -663,23 +668,26 @@ cudaError_t launch_moe(const __half* x, const float* s, const int32_t* ids, int8
 {
     constexpr int R = kThreads / G;
     const uint64_t blocks = ((uint64_t)T + R - 1) / R;
-    moe_sq_vec_kernel<G, VPT><<<(unsigned)blocks, kThreads, 0, st>>>(x, s, ids, qy, rs, T, H, K, E, qmax, perm);
-    return cudaGetLastError();
+    return launch_pdl(moe_sq_vec_kernel<G, VPT>, dim3((unsigned)blocks), dim3(kThreads), 0, st, x, s, ids, qy, rs, T, H,
+                      K, E, qmax, perm);
 }
 
 #define B2SQ_VEC_DISPATCH(FN, ...)                                        \
     switch (cfg.G * 16 + cfg.VPT) {                                       \
-        case 32 * 16 + 1: return FN<32, 1>(__VA_ARGS__);                  \
-        case 64 * 16 + 1: return FN<64, 1>(__VA_ARGS__);                  \
-        case 128 * 16 + 1: return FN<128, 1>(__VA_ARGS__);                \
-        case 256 * 16 + 1: return FN<256, 1>(__VA_ARGS__);                \
-        case 256 * 16 + 2: return FN<256, 2>(__VA_ARGS__);                \
-        case 256 * 16 + 3: return FN<256, 3>(__VA_ARGS__);                \
-        case 256 * 16 + 4: return FN<256, 4>(__VA_ARGS__);                \
-        case 256 * 16 + 5: return FN<256, 5>(__VA_ARGS__);                \
-        case 256 * 16 + 6: return FN<256, 6>(__VA_ARGS__);                \
-        case 256 * 16 + 7: return FN<256, 7>(__VA_ARGS__);                \
-        case 256 * 16 + 8: return FN<256, 8>(__VA_ARGS__);                \
+        case 32 * 16 + 1: return FN<32, 1>(__VA_ARGS__);              \
+        case 32 * 16 + 2: return FN<32, 2>(__VA_ARGS__);              \
+        case 32 * 16 + 3: return FN<32, 3>(__VA_ARGS__);              \
+        case 32 * 16 + 4: return FN<32, 4>(__VA_ARGS__);              \
+        case 64 * 16 + 3: return FN<64, 3>(__VA_ARGS__);              \
+        case 64 * 16 + 4: return FN<64, 4>(__VA_ARGS__);              \
+        case 128 * 16 + 3: return FN<128, 3>(__VA_ARGS__);            \
+        case 128 * 16 + 4: return FN<128, 4>(__VA_ARGS__);            \
+        case 256 * 16 + 3: return FN<256, 3>(__VA_ARGS__);            \
+        case 256 * 16 + 4: return FN<256, 4>(__VA_ARGS__);            \
+        case 256 * 16 + 5: return FN<256, 5>(__VA_ARGS__);            \
+        case 256 * 16 + 6: return FN<256, 6>(__VA_ARGS__);            \
+        case 256 * 16 + 7: return FN<256, 7>(__VA_ARGS__);            \
+        case 256 * 16 + 8: return FN<256, 8>(__VA_ARGS__);            \
         default: return cudaErrorInvalidValue;                            \
     }
 
@@ -742,9 +750,8 @@ cudaError_t launch_sq_tma(const __half* x, const float* s, int8_t* y, float* rs,
     unsigned grid = 0;
     cudaError_t e = persistent_grid(sq_tma_kernel<VPT>, c.smem, M, &grid);
     if (e != cudaSuccess) return e;
-    sq_tma_kernel<VPT><<<grid, kTmaThreads, c.smem, st>>>(x, s, y, rs, M, N, qmax, c.stages, c.stage_bytes,
-                                                          c.out_bytes);
-    return cudaGetLastError();
+    return launch_pdl(sq_tma_kernel<VPT>, dim3(grid), dim3(kTmaThreads), c.smem, st, x, s, y, rs, M, N, qmax, c.stages,
+                      c.stage_bytes, c.out_bytes);
 }
 
 #define B2SQ_TMA_DISPATCH(FN, VPT, ...)        \
@@ -791,8 +798,7 @@ cudaError_t launch_smoothquant(const void* x, const float* s, int8_t* y, float* 
     const bool vec_ok = (N % 8 == 0) && aligned(x, 16) && aligned(y, 8) && aligned(s, 16) && pick_cfg(N / 8, cfg);
     if (used_vector_path) *used_vector_path = vec_ok ? 1 : 0;
     if (!vec_ok) {
-        sq_generic_kernel<<<generic_grid(M), kThreads, 0, st>>>(xh, s, y, rs, M, N, qmax);
-        return cudaGetLastError();
+        return launch_pdl(sq_generic_kernel, dim3(generic_grid(M)), dim3(kThreads), 0, st, xh, s, y, rs, M, N, qmax);
     }
     uint32_t vpt = 0;
     if (use_tma(M, N, vpt)) {
@@ -811,9 +817,8 @@ cudaError_t launch_moe_smoothquant(const void* x, const float* s, const int32_t*
     const bool vec_ok = (H % 8 == 0) && aligned(x, 16) && aligned(qy, 8) && aligned(s, 16) && pick_cfg(H / 8, cfg);
     if (used_vector_path) *used_vector_path = vec_ok ? 1 : 0;
     if (!vec_ok) {
-        moe_sq_generic_kernel<<<generic_grid((uint64_t)T * K), kThreads, 0, st>>>(xh, s, ids, qy, rs, T, H, K, E,
-                                                                                  qmax, perm);
-        return cudaGetLastError();
+        return launch_pdl(moe_sq_generic_kernel, dim3(generic_grid((uint64_t)T * K)), dim3(kThreads), 0, st, xh, s, ids, qy,
+                          rs, T, H, K, E, qmax, perm);
     }
     // MoE uses the register-resident row groups at every size: a streaming
     // (TMA-staged) variant measured slower at every configuration tried (its
