@@ -4,7 +4,7 @@
 //   rocwmma_smoothquant.cpp:138-176      [SmoothQuant] M=.. N=..  X ms  Y GB/s
 //   rocwmma_moe_smoothquant.cpp:147-206  [MoE-SmoothQuant] tokens=.. ...  X ms  Y GB/s
 //   rocwmma_gemm_quantized.cpp:197-268   [QuantGEMM-I8] M=.. N=.. K=..  X ms  Y TFlops/s
-//   rocwmma_moe_sorting.cpp:141-208      [MoE-Sorting] tokens=.. experts=.. topk=.. unit=..  X ms
+//   rocwmma_moe_sorting.cpp:141-208      [MoE Sorting] tokens=.. experts=.. topk=.. unit=..  X ms  Y GB/s
 //   rocwmma_topk_softmax.cpp:197-256     [TopK-Softmax] tokens=.. experts=.. topk=..  X ms  Y GB/s
 //
 // so output parsers written for the reference (benchmark.sh:177-188) read it
@@ -225,13 +225,17 @@ static void test_moe_sorting(uint32_t tokens, uint32_t experts, uint32_t topk, u
         CHECK_B2SQ(b2sq_moe_sorting(dIds, tokens, topk, experts, unit, dCnt, dStart, dSorted, nullptr, nullptr));
     };
     const double ms = bench(fn, 3, 10);
-    std::printf("[MoE-Sorting] tokens=%u experts=%u topk=%u unit=%u  %g ms\n", tokens, experts, topk, unit, ms);
+    // rocwmma_moe_sorting.cpp:188-192: ids read + sorted ids written, padded capacity
+    const double total_topk = (double)tokens * topk, total_padded = total_topk + (double)experts * unit;
+    const double gbs = (total_topk * 4 * 2 + total_padded * 4) / (ms * 1e-3) / 1e9;
+    std::printf("[MoE Sorting] tokens=%u experts=%u topk=%u unit=%u  %g ms  %g GB/s\n", tokens, experts, topk, unit, ms,
+                gbs);
     std::vector<int32_t> hCnt(experts);
     CHECK_CUDA(cudaMemcpy(hCnt.data(), dCnt, experts * 4, cudaMemcpyDeviceToHost));
     uint64_t total = 0;
     for (int32_t c : hCnt) total += (uint64_t)c;
     if (total != hIds.size()) {
-        std::printf("[MoE-Sorting] known answer FAILED (counts do not sum to tokens*topk)\n");
+        std::printf("[MoE Sorting] known answer FAILED (counts do not sum to tokens*topk)\n");
         ++g_failures;
     }
     CHECK_CUDA(cudaFree(dIds));
