@@ -360,6 +360,17 @@ def main():
         prefill["with_collectives"] = {"ms": ms_e, "tops": ops_pf / (ms_e * 1e-3) / 1e12,
                                        "note": "rank 0 quantises, NCCL broadcast of Xq and row scales, "
                                                "sharded GEMM, NCCL all-gather of the bf16 output into [M, N]"}
+        # GEMM -> all-gather of the output: NCCL after the GEMM vs fused into the GEMM's epilogue
+        ms_g = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", True), 5)
+        ms_f = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
+        out_bytes = PM * PN * 2
+        prefill["gather_nccl"] = {"ms": ms_g, "tops": ops_pf / (ms_g * 1e-3) / 1e12,
+                                  "note": "x replicated, sharded GEMM, then NCCL all-gather into [M, N]"}
+        prefill["gather_fused"] = {"ms": ms_f, "tops": ops_pf / (ms_f * 1e-3) / 1e12,
+                                   "nvlink_bytes_out_per_gpu": out_bytes // world * (world - 1),
+                                   "note": "x replicated, b2sq_gemm_i8_allgather: the GEMM epilogue stores every "
+                                           "output tile into all ranks' [M, N] buffers over NVLink (CUDA IPC), "
+                                           "one-element all-reduce barriers before and after"}
     del layer, w_pf, x_pf
 
     # ---------------- e2e through the C ABI from pinned host buffers

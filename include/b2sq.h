@@ -209,6 +209,45 @@ B2SQ_API b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k,
                               b2sq_gemm_plan* plan);
 
 /* ------------------------------------------------------------------------ */
+/* Multi-GPU: the N-sharded GEMM fused with the output all-gather           */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Column-parallel GEMM whose epilogue performs the all-gather of the output
+ * (no counterpart in the reference, which is single-GPU; it replaces the
+ * GEMM + ncclAllGather pair of an N-sharded layer).  This rank computes its
+ * shard C_r = dequant(A x B) of n columns, exactly as b2sq_gemm_i8, and
+ * stores every output value into each rank's full output buffer:
+ *   c_ranks[j] + (row * ldc + col_offset + col) elements, for j < world,
+ * where c_ranks[rank] is this rank's own buffer and the others are peer
+ * buffers mapped into this process (b2sq_ipc_open).  The stores are plain
+ * stores over NVLink from the epilogue, overlapped with the next tiles'
+ * math; no multicast is used.  The caller orders the exchange: every rank
+ * must be done with the previous contents before any rank calls, and the
+ * gathered result is complete once every rank's call has completed (a
+ * barrier after the call, e.g. a one-element ncclAllReduce on the stream).
+ * world <= 8; all buffers share their 16-byte alignment.
+ */
+B2SQ_API b2sq_status b2sq_gemm_i8_allgather(uint32_t m, uint32_t n, uint32_t k,
+                                  const int8_t* a, b2sq_layout la, uint32_t lda,
+                                  const int8_t* b, b2sq_layout lb, uint32_t ldb,
+                                  void* const* c_ranks, uint32_t world, uint32_t rank,
+                                  uint32_t col_offset, b2sq_dtype c_type, uint32_t ldc,
+                                  const float* scale_a_row, const float* scale_b_col,
+                                  float scale_a, float scale_b,
+                                  void* workspace, size_t workspace_bytes,
+                                  b2sq_stream_t stream);
+
+/* CUDA IPC for the all-gather buffers: export a device pointer (memory from
+ * cudaMalloc, any offset inside it) as a 64-byte handle plus offset, open a
+ * peer's handle in this process (the returned base + offset is the peer's
+ * pointer), and close it again. */
+typedef struct { unsigned char bytes[64]; } b2sq_ipc_handle;
+B2SQ_API b2sq_status b2sq_ipc_export(const void* dev_ptr, b2sq_ipc_handle* handle, uint64_t* offset);
+B2SQ_API b2sq_status b2sq_ipc_open(const b2sq_ipc_handle* handle, void** base);
+B2SQ_API b2sq_status b2sq_ipc_close(void* base);
+
+/* ------------------------------------------------------------------------ */
 /* MoE: grouping by expert and the grouped (per-expert) GEMM                */
 /* ------------------------------------------------------------------------ */
 

@@ -65,6 +65,11 @@ SIGNATURES = {
                                       _vp, _f32, _vp, _sz, _vp]),
     "b2sq_gemm_i8_workspace_size": (_i, [_u32, _u32, _u32, _i, _i, C.POINTER(_sz)]),
     "b2sq_gemm_i8_plan": (_i, [_u32, _u32, _u32, _i, _i, _i, _u32, C.POINTER(GemmPlan)]),
+    "b2sq_gemm_i8_allgather": (_i, [_u32, _u32, _u32, _vp, _i, _u32, _vp, _i, _u32, _vp, _u32, _u32, _u32, _i, _u32,
+                                    _vp, _vp, _f32, _f32, _vp, C.c_size_t, _vp]),
+    "b2sq_ipc_export": (_i, [_vp, _vp, C.POINTER(C.c_uint64)]),
+    "b2sq_ipc_open": (_i, [_vp, C.POINTER(C.c_void_p)]),
+    "b2sq_ipc_close": (_i, [_vp]),
     "b2sq_topk_softmax": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "b2sq_moe_sorting": (_i, [_vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp]),
     "b2sq_gemm_i8_grouped": (_i, [_u32, _u32, _u32, _u32, _vp, _u32, _vp, _u32, _vp, _i, _u32, _vp, _vp,

@@ -226,6 +226,55 @@ gemm_quant_tensor_scale = gemm_quant
 
 
 # ----------------------------------------------------------------------------- MoE
+def gemm_allgather(a: torch.Tensor, b: torch.Tensor, c_ranks: list, rank: int, col_offset: int, ldc: int,
+                   scale_a_row: Optional[torch.Tensor] = None, scale_b_col: Optional[torch.Tensor] = None,
+                   scale_a: float = 1.0, scale_b: float = 1.0, out_dtype: torch.dtype = torch.bfloat16,
+                   workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """This rank's N shard of a column-parallel GEMM, stored into every rank's
+    full output buffer (b2sq_gemm_i8_allgather).  c_ranks: device addresses
+    (ints) of each rank's row-major [M, ldc] buffer, mapped into this process;
+    the shard lands at columns [col_offset, col_offset + N) of all of them."""
+    if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError("a int8 [M, K] and b int8 [K, N] expected")
+    M, K = a.shape
+    N = b.shape[1]
+    la, lda = _layout_of(a, M, K)
+    lb, ldb = _layout_of(b, K, N)
+    if out_dtype not in _DTYPE_CODE:
+        raise ValueError("out_dtype must be float16, bfloat16 or int32")
+    dev = _need_cuda(a, b, scale_a_row, scale_b_col)
+    need = workspace_size(M, N, K, la, lb)
+    ws = (workspace or _default_ws).get(dev, need)
+    ptrs = (C.c_void_p * len(c_ranks))(*[int(p) for p in c_ranks])
+    lib = _lib.load()
+    st = lib.b2sq_gemm_i8_allgather(M, N, K, a.data_ptr(), la, lda, b.data_ptr(), lb, ldb, ptrs, len(c_ranks), rank,
+                                    col_offset, _DTYPE_CODE[out_dtype], ldc, _ptr(scale_a_row), _ptr(scale_b_col),
+                                    float(scale_a), float(scale_b), _ptr(ws), 0 if ws is None else ws.numel(),
+                                    _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_gemm_i8_allgather")
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding t, byte offset of t in it)."""
+    _need_cuda(t)
+    h = (C.c_ubyte * 64)()
+    off = C.c_uint64(0)
+    _lib.check(_lib.load().b2sq_ipc_export(t.data_ptr(), h, C.byref(off)), "b2sq_ipc_export")
+    return bytes(h), int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Maps a peer's exported allocation into this process; returns its base address."""
+    h = (C.c_ubyte * 64).from_buffer_copy(handle)
+    base = C.c_void_p(0)
+    _lib.check(_lib.load().b2sq_ipc_open(h, C.byref(base)), "b2sq_ipc_open")
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    _lib.check(_lib.load().b2sq_ipc_close(C.c_void_p(base)), "b2sq_ipc_close")
+
+
 def topk_softmax(logits: torch.Tensor, topk: int, topk_weights: Optional[torch.Tensor] = None,
                  topk_indices: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None):
     """MoE router (rocwmma_topk_softmax.cpp): softmax over fp16 logits

@@ -9,6 +9,8 @@
 #include "../../include/b2sq.h"
 #include "kernels.h"
 
+#include <cuda.h>
+
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -236,15 +238,18 @@ namespace {
 b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
                          const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
                          const float* scale_a_row, const float* scale_b_col, float scale_a, float scale_b,
-                         void* workspace, size_t workspace_bytes, b2sq_stream_t stream, bool a_from_prev_kernel)
+                         void* workspace, size_t workspace_bytes, b2sq_stream_t stream, bool a_from_prev_kernel,
+                         void* const* extra_c = nullptr, uint32_t n_extra = 0)
 {
     b2sq_status st = validate_gemm(m, n, k, a, la, lda, b, lb, ldb, c, c_type, ldc, scale_a_row, scale_b_col);
     if (st != B2SQ_OK || m == 0 || n == 0) return st;
     cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
     const size_t esz = c_type == B2SQ_I32 ? 4 : 2;
     if (k == 0) {  // empty sum: every output is +0
-        cudaError_t e = cudaMemset2DAsync(c, (size_t)ldc * esz, 0, (size_t)n * esz, m, cs);
-        if (e != cudaSuccess) return cuda_fail(e, "gemm_i8: zero fill");
+        for (uint32_t d = 0; d <= n_extra; ++d) {
+            cudaError_t e = cudaMemset2DAsync(d == 0 ? c : extra_c[d - 1], (size_t)ldc * esz, 0, (size_t)n * esz, m, cs);
+            if (e != cudaSuccess) return cuda_fail(e, "gemm_i8: zero fill");
+        }
         return ok();
     }
     uint32_t sms = 0;
@@ -263,6 +268,8 @@ b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
     p.c_type = (int)c_type;
     p.transpose_out = (int)mp.swap;
     p.pdl_dep = a_from_prev_kernel ? (mp.swap ? 2 : 1) : 0;
+    p.n_extra = n_extra;
+    for (uint32_t d = 0; d < n_extra; ++d) p.extra_c[d] = extra_c[d];
     if (mp.swap) {
         p.a = b;
         p.lda = ldb;
@@ -296,9 +303,91 @@ b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
     }
     return ok();
 }
+// Driver-API entry points used by the IPC helpers (no link-time libcuda dependency).
+typedef CUresult (*MemGetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+MemGetAddressRangeFn get_address_range_fn()
+{
+    static MemGetAddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<MemGetAddressRangeFn>(ptr);
+    });
+    return fn;
+}
 }  // namespace
 
 extern "C" {
+
+b2sq_status b2sq_gemm_i8_allgather(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
+                                   const int8_t* b, b2sq_layout lb, uint32_t ldb, void* const* c_ranks,
+                                   uint32_t world, uint32_t rank, uint32_t col_offset, b2sq_dtype c_type,
+                                   uint32_t ldc, const float* scale_a_row, const float* scale_b_col, float scale_a,
+                                   float scale_b, void* workspace, size_t workspace_bytes, b2sq_stream_t stream)
+{
+    if (world == 0 || world > b2sq::kMaxExtraOut + 1)
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather: world must be in [1, %u]", b2sq::kMaxExtraOut + 1);
+    if (rank >= world) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather: rank %u >= world %u", rank, world);
+    if (!c_ranks) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather: c_ranks is null");
+    if ((uint64_t)col_offset + n > ldc)
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather: col_offset + n exceeds ldc");
+    const size_t esz = c_type == B2SQ_I32 ? 4 : 2;
+    void* dst[b2sq::kMaxExtraOut + 1];
+    for (uint32_t r = 0; r < world; ++r) {
+        if (!c_ranks[r]) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather: c_ranks[%u] is null", r);
+        dst[r] = static_cast<uint8_t*>(c_ranks[r]) + (size_t)col_offset * esz;
+    }
+    // Every destination gets the same stores: they must share their alignment.
+    for (uint32_t r = 1; r < world; ++r)
+        if ((reinterpret_cast<uintptr_t>(dst[r]) & 15) != (reinterpret_cast<uintptr_t>(dst[0]) & 15))
+            return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8_allgather: the output buffers differ in 16-byte alignment");
+    void* extra[b2sq::kMaxExtraOut];
+    uint32_t ne = 0;
+    for (uint32_t r = 0; r < world; ++r)
+        if (r != rank) extra[ne++] = dst[r];
+    return gemm_i8_impl(m, n, k, a, la, lda, b, lb, ldb, dst[rank], c_type, ldc, scale_a_row, scale_b_col, scale_a,
+                        scale_b, workspace, workspace_bytes, stream, false, extra, ne);
+}
+
+b2sq_status b2sq_ipc_export(const void* dev_ptr, b2sq_ipc_handle* handle, uint64_t* offset)
+{
+    if (!dev_ptr || !handle || !offset) return fail(B2SQ_ERR_INVALID_ARG, "ipc_export: null pointer");
+    MemGetAddressRangeFn range = get_address_range_fn();
+    if (!range) return fail(B2SQ_ERR_CUDA, "ipc_export: cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return fail(B2SQ_ERR_INVALID_ARG, "ipc_export: not a device allocation");
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(handle->bytes), "IPC handle size");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "ipc_export: cudaIpcGetMemHandle (memory from cudaMalloc is required)");
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *offset = reinterpret_cast<uint64_t>(dev_ptr) - (uint64_t)base;
+    return ok();
+}
+
+b2sq_status b2sq_ipc_open(const b2sq_ipc_handle* handle, void** base)
+{
+    if (!handle || !base) return fail(B2SQ_ERR_INVALID_ARG, "ipc_open: null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "ipc_open: cudaIpcOpenMemHandle");
+    return ok();
+}
+
+b2sq_status b2sq_ipc_close(void* base)
+{
+    if (!base) return fail(B2SQ_ERR_INVALID_ARG, "ipc_close: null pointer");
+    cudaError_t e = cudaIpcCloseMemHandle(base);
+    if (e != cudaSuccess) return cuda_fail(e, "ipc_close: cudaIpcCloseMemHandle");
+    return ok();
+}
 
 b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
                          const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,

@@ -59,6 +59,7 @@ constexpr uint32_t kThreads = 192;  // 6 warps
 constexpr uint32_t kEpiThreads = 128;
 constexpr uint32_t kSmemBudget = 232448;  // 227 KiB opt-in limit per CTA
 constexpr uint32_t kBarrierBytes = 256;
+constexpr uint32_t kEpiStageBytes = 4 * 4096;  // 4 epilogue warps x (32 rows x 128 B)
 
 // K depth of a pipeline stage for a tile width.
 __host__ __device__ constexpr uint32_t tile_k_for(uint32_t bn) { return bn <= 32 ? 512 : bn <= 64 ? 256 : 128; }
@@ -85,6 +86,8 @@ struct KParams {
     int c_type;
     int transpose_out;
     int vec_store_ok;
+    void* extra_c[kMaxExtraOut];  // further destinations of every store (all-gather)
+    uint32_t n_extra;
     const float* row_scale_vec;
     const float* col_scale_vec;
     float row_scale, col_scale;
@@ -222,7 +225,12 @@ struct Smem {
     static constexpr uint32_t taddr_off = tempty_off + 16;
     static constexpr uint32_t abort_off = taddr_off + 4;
     static constexpr uint32_t flag_off = abort_off + 4;
-    static constexpr uint32_t total = bar_off + kBarrierBytes + 1024;
+    // 4 KiB per epilogue warp to re-shape output chunks for coalesced stores
+    // to peer GPUs (all-gather), when the pipeline leaves room for it.
+    static constexpr uint32_t epi_off = bar_off + kBarrierBytes;
+    static constexpr uint32_t EPI =
+        (bar_off + kBarrierBytes + kEpiStageBytes + 1024 <= kSmemBudget) ? kEpiStageBytes : 0;
+    static constexpr uint32_t total = bar_off + kBarrierBytes + EPI + 1024;
     static_assert(ST >= 2, "pipeline needs at least two stages");
     static_assert(flag_off + 4 <= bar_off + kBarrierBytes, "barrier area overflow");
     static_assert(total <= kSmemBudget, "shared memory overflow");
@@ -247,26 +255,14 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, int32_t (&acc)[W])
     else tmem_ld_32x32b_x16(taddr, reinterpret_cast<uint32_t(&)[16]>(acc));
 }
 
-// Dequantises and stores W consecutive kernel columns [col0, col0+W) of
-// kernel row `row` (one thread = one row).  rsc is this row's scale;
-// csc_lane is the scale of column col0 + (lane % W), so the warp holds the
-// chunk's column scales in one register and shares them by shuffles.
-// Called by all 32 lanes of a warp (the shuffles precede any early exit).
+// Stores one dequantised chunk (v, or the raw acc for int32 output) of kernel
+// row `row` into the output buffer at cbase.
 template <uint32_t W>
-__device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&acc)[W],
-                                            float rsc, float csc_lane)
+__device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t row, uint32_t col0,
+                                         const int32_t (&acc)[W], const float (&v)[W])
 {
-    float v[W];
-    if (p.c_type != 2) {
-#pragma unroll
-        for (int j = 0; j < (int)W; ++j) {
-            const float csc = __shfl_sync(0xffffffffu, csc_lane, j);
-            v[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(rsc, csc));
-        }
-    }
-    if (row >= p.Mk) return;
     if (p.c_type == 2) {  // raw int32
-        int32_t* c = static_cast<int32_t*>(p.c);
+        int32_t* c = static_cast<int32_t*>(cbase);
         if (!p.transpose_out) {
             int32_t* dst = c + (size_t)row * p.ldc + col0;
             if (p.vec_store_ok && col0 + W <= p.Nk) {
@@ -285,7 +281,7 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
         }
         return;
     }
-    uint16_t* c = static_cast<uint16_t*>(p.c);
+    uint16_t* c = static_cast<uint16_t*>(cbase);
     if (!p.transpose_out) {
         uint16_t* dst = c + (size_t)row * p.ldc + col0;
         if (p.vec_store_ok && col0 + W <= p.Nk) {
@@ -319,6 +315,102 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
             }
         }
     }
+}
+
+
+// Dequantises and stores W consecutive kernel columns [col0, col0+W) of
+// kernel row `row` (one thread = one row).  rsc is this row's scale;
+// csc_lane is the scale of column col0 + (lane % W), so the warp holds the
+// chunk's column scales in one register and shares them by shuffles.
+// Called by all 32 lanes of a warp (the shuffles precede any early exit).
+template <uint32_t W>
+__device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&acc)[W],
+                                            float rsc, float csc_lane)
+{
+    float v[W];
+    if (p.c_type != 2) {
+#pragma unroll
+        for (int j = 0; j < (int)W; ++j) {
+            const float csc = __shfl_sync(0xffffffffu, csc_lane, j);
+            v[j] = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(rsc, csc));
+        }
+    }
+    if (row >= p.Mk) return;
+    for (uint32_t d = 0; d <= p.n_extra; ++d) {
+        void* const cbase = d == 0 ? p.c : p.extra_c[d - 1];
+        store_to(p, cbase, row, col0, acc, v);
+    }
+}
+
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 lds128_epi(uint32_t addr)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Two consecutive W-column chunks of the warp's 32 rows.  With extra (peer)
+// destinations, a 16-bit output and room to stage (stage = this warp's 4 KiB
+// of shared memory, 0 if none), the 32 x 64 values are re-shaped through
+// shared memory so that every store instruction writes 4 rows x 128
+// contiguous bytes: NVLink moves peer stores at full rate only from 128-byte
+// runs per instruction (measured on B200: 16-byte runs reach a quarter of
+// it), while local stores are combined in L2 either way.  Same values as
+// store_chunk in every case.
+template <uint32_t W>
+__device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&a0)[W],
+                                           const int32_t (&a1)[W], float rsc, float cs0, float cs1, uint32_t stage)
+{
+    if constexpr (W == 32) {
+        if (stage != 0 && p.n_extra > 0 && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
+            col0 + 2 * W <= p.Nk) {
+            const uint32_t lane = threadIdx.x & 31;
+            uint32_t w[32];  // this row's 64 outputs, packed in pairs
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float c0 = __shfl_sync(0xffffffffu, cs0, j), c1 = __shfl_sync(0xffffffffu, cs0, j + 1);
+                const float v0 = __fmul_rn(__int2float_rn(a0[j]), __fmul_rn(rsc, c0));
+                const float v1 = __fmul_rn(__int2float_rn(a0[j + 1]), __fmul_rn(rsc, c1));
+                w[j / 2] = p.c_type == 1 ? pack_bf16(v0, v1) : pack_f16(v0, v1);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float c0 = __shfl_sync(0xffffffffu, cs1, j), c1 = __shfl_sync(0xffffffffu, cs1, j + 1);
+                const float v0 = __fmul_rn(__int2float_rn(a1[j]), __fmul_rn(rsc, c0));
+                const float v1 = __fmul_rn(__int2float_rn(a1[j + 1]), __fmul_rn(rsc, c1));
+                w[16 + j / 2] = p.c_type == 1 ? pack_bf16(v0, v1) : pack_f16(v0, v1);
+            }
+            // row-major [32 rows][128 B], 16-byte pieces XOR-swizzled by row (conflict-free both ways)
+#pragma unroll
+            for (uint32_t c = 0; c < 8; ++c)
+                sts128(stage + lane * 128 + ((c ^ (lane & 7)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                       w[4 * c + 3]);
+            __syncwarp();
+            const size_t ldc_bytes = (size_t)p.ldc * 2;
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k) {
+                const uint32_t r = 4 * k + (lane >> 3), c = lane & 7;
+                const uint4 val = lds128_epi(stage + r * 128 + ((c ^ (r & 7)) << 4));
+                const uint32_t row_r = __shfl_sync(0xffffffffu, row, r);
+                if (row_r < p.Mk) {
+                    const size_t off = (size_t)row_r * ldc_bytes + (size_t)col0 * 2 + c * 16;
+                    *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.c) + off) = val;
+                    for (uint32_t d = 0; d < p.n_extra; ++d)
+                        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.extra_c[d]) + off) = val;
+                }
+            }
+            __syncwarp();  // the next pair rewrites the staging area
+            return;
+        }
+    }
+    store_chunk<W>(p, row, col0, a0, rsc, cs0);
+    store_chunk<W>(p, row, col0 + W, a1, rsc, cs1);
 }
 
 template <uint32_t BN, uint32_t BK, bool kGrouped>
@@ -531,6 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.pdl_dep) griddep_wait();  // row scales come from the previous kernel
         const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
         const uint32_t row_local = q * 32 + lane;
+        const uint32_t epi_stage = L::EPI ? sbase + L::epi_off + q * 4096 : 0u;
         const uint32_t ethread = threadIdx.x - 64;
         UnitIter it;
         it.init(p, tiles_total);
@@ -584,8 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __syncwarp();
                             if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
                         }
-                        store_chunk<CW>(p, row, tn_col0 + ch * CW, acc0, rsc, csv[ch]);
-                        store_chunk<CW>(p, row, tn_col0 + (ch + 1) * CW, acc1, rsc, csv[ch + 1]);
+                        store_pair<CW>(p, row, tn_col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
                     }
                 }
             } else {
@@ -680,7 +772,8 @@ constexpr uint32_t kPairHalfBytes = 128 * kPairBK;          // 16 KiB: one opera
 constexpr uint32_t kPairSB = 2 * kPairHalfBytes;            // A half + B half per CTA per stage
 constexpr uint32_t kPairST = 6;
 constexpr uint32_t kPairBarOff = kPairST * kPairSB;
-constexpr uint32_t kPairSmem = kPairBarOff + kBarrierBytes + 1024;
+constexpr uint32_t kPairEpiOff = kPairBarOff + kBarrierBytes;
+constexpr uint32_t kPairSmem = kPairBarOff + kBarrierBytes + kEpiStageBytes + 1024;
 static_assert(kPairSmem <= kSmemBudget, "pair kernel shared memory overflow");
 
 __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
@@ -797,6 +890,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         const uint32_t q = warp & 3;
         const uint32_t row_local = q * 32 + lane;
         constexpr uint32_t CW = 32, NCH = kPairBN / CW;
+        const uint32_t epi_stage = sbase + kPairEpiOff + q * 4096;
         uint32_t uidx = 0;
         for (uint32_t t = pair; t < T; t += npairs, ++uidx) {
             const uint32_t buf = uidx & 1, use = uidx >> 1;
@@ -824,8 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
                 }
-                store_chunk<CW>(p, row, tn * kPairBN + ch * CW, acc0, rsc, csv[ch]);
-                store_chunk<CW>(p, row, tn * kPairBN + (ch + 1) * CW, acc1, rsc, csv[ch + 1]);
+                store_pair<CW>(p, row, tn * kPairBN + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
             }
         }
     }
@@ -1031,6 +1124,8 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.a_mn_major = p.a_mn_major;
     kp.b_mn_major = p.b_mn_major;
     kp.c = p.c;
+    kp.n_extra = p.n_extra;
+    for (uint32_t d = 0; d < p.n_extra && d < kMaxExtraOut; ++d) kp.extra_c[d] = p.extra_c[d];
     kp.ldc = p.ldc;
     kp.c_type = p.c_type;
     kp.transpose_out = p.transpose_out;

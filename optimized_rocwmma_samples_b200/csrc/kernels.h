@@ -19,6 +19,8 @@ cudaError_t launch_moe_smoothquant(const void* x, const float* s, const int32_t*
 
 // GEMM problem after the host has mapped the user's (A, B, layouts) onto the
 // kernel's operands: kernel A has Mk rows, kernel B has Nk rows, both K long.
+constexpr uint32_t kMaxExtraOut = 7;  // all-gather over at most 8 GPUs
+
 struct GemmProblem {
     uint32_t Mk, Nk, K;
     const int8_t* a;  // kernel A operand
@@ -33,6 +35,11 @@ struct GemmProblem {
     const float* col_scale_vec;  // per kernel-column scale (nullable)
     float row_scale, col_scale;  // used when the vector is null
     int pdl_dep;                 // 1 / 2: A / B (and row scales) come from the previous kernel (PDL)
+    // Extra output buffers (the all-gather entry): every value stored to c is
+    // also stored, at the same offset, to each of these (peer GPUs' buffers
+    // mapped into this process; plain stores over NVLink).
+    void* extra_c[kMaxExtraOut];
+    uint32_t n_extra;
 };
 
 struct GemmSchedule {

@@ -10,8 +10,11 @@ torch.distributed (NCCL on GPUs) for the exchange steps:
      broadcasts Xq (int8, half the bytes of fp16 x) and the row scales;
   2. each rank runs the GEMM on its N shard (no communication);
   3. optionally all-gather the output shards into the full row-major [M, N]
-     (``gather_output=True``); otherwise the output stays N-sharded, as a
-     column-parallel layer's output normally does.
+     (``gather_output=True``: GEMM, then NCCL all-gather, or
+     ``gather_output="fused"``: one GEMM whose epilogue stores every output
+     tile into all ranks' [M, N] buffers over NVLink, b2sq_gemm_i8_allgather);
+     otherwise the output stays N-sharded, as a column-parallel layer's
+     output normally does.
 
 The compute steps are injected (``ops``) so the same host logic runs with the
 library's CUDA kernels on GPUs and with a CPU implementation on ``gloo`` ranks
@@ -39,18 +42,72 @@ def shard_range(n: int, world: int, rank: int, align: int = SHARD_ALIGN) -> tupl
 
 @dataclass
 class Ops:
-    """Compute steps: smoothquant(x, s) -> (xq, row_scale); gemm(xq, w_shard_nk, sa, sb) -> out."""
+    """Compute steps: smoothquant(x, s) -> (xq, row_scale); gemm(xq, w_shard_nk, sa, sb) -> out;
+    gemm_gather(xq, w_shard_nk, sa, sb, n0, n_total, layer) -> the gathered [M, n_total] output."""
     smoothquant: Callable
     gemm: Callable
+    gemm_gather: Optional[Callable] = None
+
+
+class PeerOutput:
+    """A row-major [M, N] output buffer on every rank, each mapped into every
+    other rank's process by CUDA IPC, so one GEMM epilogue can store its shard
+    into all of them.  Collective to create (handles travel by
+    all_gather_object); close() unmaps the peers' buffers."""
+
+    def __init__(self, m: int, n_total: int, dtype: torch.dtype, device: torch.device, group, world: int, rank: int):
+        from . import api
+
+        self.local = torch.empty((m, n_total), dtype=dtype, device=device)
+        mine = api.ipc_export(self.local)
+        every = [None] * world
+        dist.all_gather_object(every, mine, group=group)
+        self.bases, self.ptrs = [], []
+        for r, (handle, offset) in enumerate(every):
+            if r == rank:
+                self.ptrs.append(self.local.data_ptr())
+            else:
+                base = api.ipc_open(handle)
+                self.bases.append(base)
+                self.ptrs.append(base + offset)
+
+    def close(self):
+        from . import api
+
+        for b in self.bases:
+            api.ipc_close(b)
+        self.bases, self.ptrs = [], []
 
 
 def cuda_ops(out_dtype: torch.dtype = torch.bfloat16) -> Ops:
     from . import api
 
     ws = api.Workspace()
+    peers: dict = {}
+    flag: dict = {}
+
+    def barrier(layer, dev):
+        # one-element all-reduce on the current stream: ordered after this
+        # rank's kernels, complete only once every rank has reached it
+        if dev not in flag:
+            flag[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+        dist.all_reduce(flag[dev], group=layer.group)
+
+    def gemm_gather(xq, w, sa, sb, n0, n_total, layer):
+        m = xq.shape[0]
+        key = (m, n_total, xq.device)
+        if key not in peers:
+            peers[key] = PeerOutput(m, n_total, out_dtype, xq.device, layer.group, layer.world, layer.rank)
+        po = peers[key]
+        barrier(layer, xq.device)  # every rank is done with the previous contents
+        api.gemm_allgather(xq, w.t(), po.ptrs, layer.rank, n0, n_total, sa, sb, out_dtype=out_dtype, workspace=ws)
+        barrier(layer, xq.device)  # every shard has landed in every buffer
+        return po.local
+
     return Ops(
         smoothquant=lambda x, s: api.smoothquant(x, s),
         gemm=lambda xq, w, sa, sb: api.gemm_quant(xq, w.t(), sa, sb, out_dtype=out_dtype, workspace=ws),
+        gemm_gather=gemm_gather,
     )
 
 
@@ -106,7 +163,14 @@ class ShardedPrefill:
         return torch.cat([p[:, :w_] for p, w_ in zip(parts, widths)], dim=1)
 
     def forward(self, x: Optional[torch.Tensor], smooth: torch.Tensor, m: int, k: int,
-                x_source: str = "replicated", gather_output: bool = False) -> torch.Tensor:
+                x_source: str = "replicated", gather_output=False) -> torch.Tensor:
+        """gather_output: False (N-sharded result), True (GEMM then all-gather)
+        or "fused" (the GEMM's epilogue gathers; the returned buffer is reused
+        by the next fused call of the same shape)."""
         xq, rs = self.quantize(x, smooth, x_source, m, k)
+        if gather_output == "fused" and self.world > 1:
+            if self.ops.gemm_gather is None:
+                raise ValueError("these ops have no fused GEMM + all-gather step")
+            return self.ops.gemm_gather(xq, self.w, rs, self.sb, self.shards[self.rank][0], self.n_total, self)
         out = self.ops.gemm(xq, self.w, rs, self.sb)
         return self.gather(out) if gather_output else out

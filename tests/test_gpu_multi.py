@@ -1,0 +1,83 @@
+"""Two GPUs (skipped with fewer): the fused GEMM + all-gather
+(b2sq_gemm_i8_allgather through ShardedPrefill, peer buffers mapped by CUDA
+IPC, plain NVLink stores from the epilogue) must give every rank the same
+[M, N] output as the single-GPU GEMM and as GEMM + NCCL all-gather, bit for
+bit, over repeated calls that reuse the buffers.  One process per GPU, NCCL."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(512, 1024, 4096), (300, 2048, 2816), (16, 8192, 4096)]  # (M, K, N); N = 2816: unequal 256-wide shards
+
+
+def worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path[:0] = [str(root), str(root / "oracle")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from optimized_rocwmma_samples_b200 import api, synth
+        from optimized_rocwmma_samples_b200.sharded import ShardedPrefill, cuda_ops, shard_range
+
+        dev = torch.device("cuda", rank)
+        res = []
+        for (M, K, N) in SHAPES:
+            ops = cuda_ops(torch.bfloat16)
+            w = synth.torch_int8_uniform((N, K), dev, 7)  # identical on every rank (seeded)
+            sb = synth.torch_scales(N, dev, 8)
+            n0, n1 = shard_range(N, world, rank)
+            layer = ShardedPrefill(w[n0:n1].contiguous(), sb[n0:n1].contiguous(), N, ops)
+            for it in range(3):
+                g = torch.Generator(device=dev)
+                g.manual_seed(100 + it)
+                x = (torch.randn((M, K), generator=g, device=dev) * 3).to(torch.float16)
+                s = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
+                fused = layer.forward(x, s, M, K, "replicated", "fused").clone()
+                nccl = layer.forward(x, s, M, K, "replicated", True)
+                xq, rs = api.smoothquant(x, s)
+                single = api.gemm_quant(xq, w.t(), rs, sb, out_dtype=torch.bfloat16)
+                torch.cuda.synchronize()
+                res.append((M, K, N, it, bool(torch.equal(fused, single)), bool(torch.equal(nccl, single))))
+        q.put((rank, res, api.last_device_error()))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e), -1))
+    finally:
+        dist.destroy_process_group()
+
+
+def free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+@pytest.mark.timeout(600)
+def test_fused_gemm_allgather_two_gpus():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=400) for _ in range(world)]
+    for p in procs:
+        p.join(60)
+    for rank, res, dev_err in results:
+        assert isinstance(res, list), f"rank {rank}: {res}"
+        assert dev_err == 0
+        for M, K, N, it, ok_fused, ok_nccl in res:
+            assert ok_fused, f"rank {rank}: fused all-gather differs at {(M, K, N)} call {it}"
+            assert ok_nccl, f"rank {rank}: NCCL all-gather differs at {(M, K, N)} call {it}"

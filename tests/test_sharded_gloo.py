@@ -39,7 +39,12 @@ def oracle_ops():
         bits = O.dequant(acc, sa.numpy(), sb.numpy(), out_dtype="bf16")
         return torch.from_numpy(bits.view(np.int16))
 
-    return Ops(smoothquant=sq, gemm=gemm)
+    # the fused GEMM + all-gather step, restated as GEMM then gather (its contract)
+    def gemm_gather(xq, w, sa, sb, n0, n_total, layer):
+        assert layer.shards[layer.rank][0] == n0 and layer.n_total == n_total
+        return layer.gather(gemm(xq, w, sa, sb))
+
+    return Ops(smoothquant=sq, gemm=gemm, gemm_gather=gemm_gather)
 
 
 def worker(rank, world, port, q):
@@ -60,6 +65,7 @@ def worker(rank, world, port, q):
         xin = torch.from_numpy(x) if rank == 0 else None
         out["rank0_gather"] = layer.forward(xin, torch.from_numpy(s), M, K, "rank0", True)
         out["rank0_shard"] = layer.forward(xin, torch.from_numpy(s), M, K, "rank0", False)
+        out["repl_fused"] = layer.forward(torch.from_numpy(x), torch.from_numpy(s), M, K, "replicated", "fused")
         q.put((rank, {k: v.numpy() for k, v in out.items()}, (n0, n1)))
     finally:
         dist.destroy_process_group()
@@ -102,3 +108,4 @@ def test_two_rank_sharded_prefill_matches_single_process():
         assert np.array_equal(out["repl_gather"], full)
         assert np.array_equal(out["rank0_gather"], full)
         assert np.array_equal(out["rank0_shard"], full[:, n0:n1])
+        assert np.array_equal(out["repl_fused"], full)
