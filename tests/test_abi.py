@@ -150,3 +150,26 @@ def test_moe_entry_points_validation_without_gpu():
                                     None) == _lib.B2SQ_ERR_INVALID_ARG  # lda < k
     assert lib.b2sq_gemm_i8_grouped(2, 16, 16, 24, (p + 15) & ~15, 24, (p + 15) & ~15, 32, p, 1, 16, None, None, 1, 1,
                                     p, p, None) == _lib.B2SQ_ERR_UNSUPPORTED  # lda % 16
+
+
+def test_allgather_and_ipc_validation_without_gpu():
+    lib = _lib.load()
+    buf = (C.c_int8 * 256)()
+    p = (C.addressof(buf) + 15) & ~15
+    two = (C.c_void_p * 2)(p, p)
+    args = (16, 16, 16, p, 0, 16, p, 1, 16)
+    tail = (None, None, 1.0, 1.0, None, 0, None)
+    assert lib.b2sq_gemm_i8_allgather(*args, two, 0, 0, 0, 1, 16, *tail) == _lib.B2SQ_ERR_INVALID_ARG  # world 0
+    assert lib.b2sq_gemm_i8_allgather(*args, two, 9, 0, 0, 1, 16, *tail) == _lib.B2SQ_ERR_INVALID_ARG  # world > 8
+    assert lib.b2sq_gemm_i8_allgather(*args, two, 2, 2, 0, 1, 16, *tail) == _lib.B2SQ_ERR_INVALID_ARG  # rank
+    assert lib.b2sq_gemm_i8_allgather(*args, None, 2, 0, 0, 1, 16, *tail) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_gemm_i8_allgather(*args, two, 2, 0, 8, 1, 16, *tail) == _lib.B2SQ_ERR_INVALID_ARG  # off + n > ldc
+    nul = (C.c_void_p * 2)(p, None)
+    assert lib.b2sq_gemm_i8_allgather(*args, nul, 2, 0, 0, 1, 16, *tail) == _lib.B2SQ_ERR_INVALID_ARG
+    skew = (C.c_void_p * 2)(p, p + 2)  # destinations must share their 16-byte alignment
+    assert lib.b2sq_gemm_i8_allgather(*args, skew, 2, 0, 0, 1, 16, *tail) == _lib.B2SQ_ERR_UNSUPPORTED
+    h = (C.c_ubyte * 64)()
+    off = C.c_uint64(0)
+    assert lib.b2sq_ipc_export(None, h, C.byref(off)) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_ipc_open(None, None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert lib.b2sq_ipc_close(None) == _lib.B2SQ_ERR_INVALID_ARG
