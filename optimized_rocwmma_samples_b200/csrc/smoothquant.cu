@@ -708,7 +708,8 @@ namespace {
 // (crossover measured on B200: at 3328 x 4096 the register-resident kernel is
 // faster, from 3328 x 8192 up the streaming one)
 constexpr uint64_t kTmaMinElems = 1ull << 24;
-constexpr uint32_t kTmaRingBytes = 110 * 1024;  // input ring per CTA: two CTAs per SM for 16 KiB rows
+constexpr uint32_t kTmaRingBytes = 110 * 1024;   // rows up to half of this take the streaming kernel
+constexpr uint32_t kTmaRingTarget = 52 * 1024;   // input ring per CTA
 
 struct TmaCfg {
     uint32_t stages, stage_bytes, out_bytes, smem;
@@ -720,8 +721,12 @@ TmaCfg tma_cfg(uint32_t row_elems, const void* y)
 {
     TmaCfg c;
     c.stage_bytes = (row_elems * 2 + 127) & ~127u;
-    const uint32_t s = kTmaRingBytes / c.stage_bytes;
-    c.stages = s < 2 ? 2 : (s > (uint32_t)kTmaMaxStages ? (uint32_t)kTmaMaxStages : s);
+    // About 52 KiB of ring, at least three rows: the consumers' per-row
+    // latency, not the loads, bounds this kernel, so more resident CTAs (rows
+    // being consumed at once) beat a deeper ring (measured at 16384 x 8192:
+    // three 16 KiB stages, 3 CTAs per SM, 2.5% faster than six, 2 per SM).
+    const uint32_t s = kTmaRingTarget / c.stage_bytes;
+    c.stages = s < 3 ? 3 : (s > (uint32_t)kTmaMaxStages ? (uint32_t)kTmaMaxStages : s);
     c.out_bytes = (row_elems % 16 == 0 && aligned(y, 16)) ? row_elems : 0;
     c.smem = c.stages * c.stage_bytes + kTmaReserved + 2 * ((c.out_bytes + 127) & ~127u);
     return c;
