@@ -373,6 +373,38 @@ def main():
                                            "one-element all-reduce barriers before and after"}
     del layer, w_pf, x_pf
 
+    # ---------------- config 5: MoE, router -> sorting -> MoE smoothquant -> grouped GEMM (replicas)
+    T5, H5, E5, K5, N5 = synth.MOE_TOKENS, synth.MOE_HIDDEN, synth.MOE_EXPERTS, synth.MOE_TOPK, synth.MOE_INTER
+    logits5 = torch.randn((T5, E5), generator=g, device=dev).to(torch.float16)
+    x5 = torch.randn((T5, H5), generator=g, device=dev).to(torch.float16)
+    s5 = torch.empty((E5, H5), device=dev).uniform_(0.5, 2.0, generator=g)
+    w5 = synth.torch_int8_uniform((E5, N5, H5), dev, 55)
+    sb5 = synth.torch_scales(E5 * N5, dev, 56)
+    unit5 = 128  # expert segments padded to whole 128-row tiles
+    tw5, ti5 = api.topk_softmax(logits5, K5)
+    cnt5, st5, sid5, perm5 = api.moe_sorting(ti5, E5, unit5)
+    rows5 = T5 * K5 + E5 * unit5
+    qy5 = torch.zeros((rows5, H5), dtype=torch.int8, device=dev)
+    rs5 = torch.zeros((rows5,), dtype=torch.float32, device=dev)
+    out5 = torch.empty((rows5, N5), dtype=torch.bfloat16, device=dev)
+
+    def moe_step():
+        api.topk_softmax(logits5, K5, tw5, ti5)
+        cnt, st, _, perm = api.moe_sorting(ti5, E5, unit5)
+        api.moe_smoothquant(x5, s5, ti5, qy=qy5, row_scale=rs5, row_perm=perm, out_rows=rows5)
+        api.gemm_grouped(qy5, w5, st, cnt, rs5, sb5, out_dtype=torch.bfloat16, c=out5)
+
+    ms_moe = timed(moe_step, 10)
+    ms_grp = timed(lambda: api.gemm_grouped(qy5, w5, st5, cnt5, rs5, sb5, out_dtype=torch.bfloat16, c=out5), 10)
+    ops5 = 2.0 * T5 * K5 * N5 * H5
+    moe = {"shape": {"tokens": T5, "hidden": H5, "experts": E5, "topk": K5, "inter": N5},
+           "pipeline_ms": ms_moe, "grouped_gemm_ms": ms_grp,
+           "grouped_gemm_tops": ops5 / (ms_grp * 1e-3) / 1e12, "pipeline_tops": ops5 / (ms_moe * 1e-3) / 1e12,
+           "gpu_launches_per_step": 4,
+           "note": "router (b2sq_topk_softmax) -> b2sq_moe_sorting -> MoE smoothquant into expert order -> "
+                   "b2sq_gemm_i8_grouped, all on the device; replicas at N > 1"}
+    del w5, qy5, out5
+
     # ---------------- e2e through the C ABI from pinned host buffers
     h_a = a.cpu().pin_memory()
     h_w = w.cpu().pin_memory()
@@ -434,6 +466,7 @@ def main():
                             "frac_of_measured_hbm": sq_gbs / hbm_gbs, "hbm_peak_gbs": hbm_gbs},
             "decode": decode,
             "prefill_c4": prefill,
+            "moe_c5": moe,
             "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
