@@ -776,6 +776,48 @@ constexpr uint32_t kPairEpiOff = kPairBarOff + kBarrierBytes;
 constexpr uint32_t kPairSmem = kPairBarOff + kBarrierBytes + kEpiStageBytes + 1024;
 static_assert(kPairSmem <= kSmemBudget, "pair kernel shared memory overflow");
 
+// One pair tile: 256 rows from a_row (rows from row_end on are not stored),
+// 256 columns from col0 of the product, B rows from b_row, column scales
+// offset by cs_off.  Grouped (MoE) mode: the tiles of group g are
+// ceil(count_g / 256) x tiles_n, M fastest, found by binary search of `gpre`.
+struct PairTile {
+    uint32_t a_row, row_end, b_row, col0, cs_off;
+};
+
+template <bool kGrouped>
+__device__ __forceinline__ PairTile pair_tile(const KParams& p, uint32_t t, const uint32_t* gpre)
+{
+    PairTile g;
+    if constexpr (kGrouped) {
+        uint32_t lo = 0, hi = p.groups;  // gpre[lo] <= t < gpre[hi]
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (gpre[mid] <= t) lo = mid;
+            else hi = mid;
+        }
+        const uint32_t tl = t - gpre[lo];
+        const uint32_t cnt = (uint32_t)p.grp_count[lo];
+        const uint32_t tme = (cnt + 255) / 256;
+        const uint32_t tm = tl % tme, tn = tl / tme;
+        const uint32_t start = (uint32_t)p.grp_start[lo];
+        g.a_row = start + tm * 256;
+        g.row_end = start + cnt;
+        g.b_row = lo * p.Nk + tn * kPairBN;
+        g.col0 = tn * kPairBN;
+        g.cs_off = lo * p.Nk;
+    } else {
+        uint32_t tm, tn;
+        tile_coords(p, t, tm, tn);
+        g.a_row = tm * 256;
+        g.row_end = p.Mk;
+        g.b_row = tn * kPairBN;
+        g.col0 = tn * kPairBN;
+        g.cs_off = 0;
+    }
+    return g;
+}
+
+template <bool kGrouped>
 __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const KParams p, uint64_t wait_limit_ns)
@@ -797,7 +839,23 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     const uint32_t rank = cluster_ctarank();
     const uint32_t pair = blockIdx.x >> 1;
     const uint32_t npairs = gridDim.x >> 1;
-    const uint32_t T = p.tiles_m * p.tiles_n;
+    uint32_t T = p.tiles_m * p.tiles_n;
+    const uint32_t* gpre = nullptr;  // grouped mode: pair-tile prefix per group, [groups + 1]
+    if constexpr (kGrouped) {
+        __shared__ uint32_t s_gpre[kMaxGroups + 1];
+        if (threadIdx.x == 0) {
+            uint32_t acc = 0;
+            for (uint32_t g = 0; g < p.groups; ++g) {
+                s_gpre[g] = acc;
+                const uint32_t cnt = p.grp_count[g] > 0 ? (uint32_t)p.grp_count[g] : 0u;
+                acc += ((cnt + 255) / 256) * p.tiles_n;
+            }
+            s_gpre[p.groups] = acc;
+        }
+        __syncthreads();
+        gpre = s_gpre;
+        T = s_gpre[p.groups];
+    }
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < ST; ++s) {
@@ -829,10 +887,9 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             uint32_t stage = 0, phase = 0;
             bool ok = true;
             for (uint32_t t = pair; ok && t < T; t += npairs) {
-                uint32_t tm, tn;
-                tile_coords(p, t, tm, tn);
-                const int32_t a_row = (int32_t)(tm * 256 + rank * 128);
-                const int32_t b_row = (int32_t)(tn * kPairBN + rank * 128);
+                const PairTile tg = pair_tile<kGrouped>(p, t, gpre);
+                const int32_t a_row = (int32_t)(tg.a_row + rank * 128);
+                const int32_t b_row = (int32_t)(tg.b_row + rank * 128);
                 for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
                     if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
                         ok = false;
@@ -896,16 +953,18 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             const uint32_t buf = uidx & 1, use = uidx >> 1;
             if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) break;
             tc_fence_after();
-            uint32_t tm, tn;
-            tile_coords(p, t, tm, tn);
-            const uint32_t row = tm * 256 + rank * 128 + row_local;
+            const PairTile tg = pair_tile<kGrouped>(p, t, gpre);
+            // rows past the tile's limit (the matrix, or the group) get an
+            // out-of-range index so the stores skip them
+            const uint32_t row0 = tg.a_row + rank * 128 + row_local;
+            const uint32_t row = row0 < tg.row_end ? row0 : 0xffffffffu;
             const uint32_t taddr = tmem_base + ((q * 32) << 16) + buf * kPairBN;
             const float rsc = (p.row_scale_vec && row < p.Mk) ? __ldg(p.row_scale_vec + row) : p.row_scale;
             float csv[NCH];
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ++ch) {
-                const uint32_t col = tn * kPairBN + ch * CW + lane;
-                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + col) : 0.f) : p.col_scale;
+                const uint32_t col = tg.col0 + ch * CW + lane;
+                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f) : p.col_scale;
             }
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ch += 2) {
@@ -918,7 +977,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
                 }
-                store_pair<CW>(p, row, tn * kPairBN + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
+                store_pair<CW>(p, row, tg.col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
             }
         }
     }
@@ -1015,6 +1074,7 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     return cudaGetLastError();
 }
 
+template <bool kGrouped>
 cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
     static std::atomic<uint64_t> done_mask{0};
@@ -1023,11 +1083,11 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_pair_kernel<<<kp.ctas, kThreads, kPairSmem, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_pair_kernel<kGrouped><<<kp.ctas, kThreads, kPairSmem, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -1142,7 +1202,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.raster_group = B2SQ_RASTER_GROUP;
     kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
-    if (s.cta_pair) return launch_pair(ta, tb, kp, st);
+    if (s.cta_pair) return launch_pair<false>(ta, tb, kp, st);
     switch (bn) {
         case 16: return launch_tile<16, tile_k_for(16)>(ta, tb, kp, st);
         case 32: return launch_tile<32, tile_k_for(32)>(ta, tb, kp, st);
@@ -1158,9 +1218,13 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
 cudaError_t launch_gemm_i8_grouped(const GroupedProblem& g, uint32_t num_sms, cudaStream_t st, const char** detail)
 {
     constexpr uint32_t BN = 256;
+    // CTA pairs (256 x 256 tiles) whenever there are two SMs: a 1-CTA 128 x
+    // 256 tile streams 1.5x the operand bytes per MMA and was L2-bound at
+    // config 5 (57% tensor utilisation, against 84% for pairs).
+    const bool pairs = num_sms != 1;
     CUtensorMap ta, tb;
     if (!make_operand_map(&ta, g.a, g.rows, g.K, g.lda, false, kTileM) ||
-        !make_operand_map(&tb, g.b, g.groups * g.N, g.K, g.ldb, false, BN)) {
+        !make_operand_map(&tb, g.b, g.groups * g.N, g.K, g.ldb, false, pairs ? 128 : BN)) {
         if (detail) *detail = "cuTensorMapEncodeTiled rejected an operand (alignment / stride)";
         return cudaErrorInvalidValue;
     }
@@ -1187,6 +1251,11 @@ cudaError_t launch_gemm_i8_grouped(const GroupedProblem& g, uint32_t num_sms, cu
     kp.grp_start = g.group_start;
     kp.grp_count = g.group_count;
     kp.groups = g.groups;
+    if (pairs) {
+        kp.k_blocks = (g.K + kPairBK - 1) / kPairBK;
+        kp.ctas = 2 * ((num_sms ? num_sms : 148) / 2);
+        return launch_pair<true>(ta, tb, kp, st);
+    }
     return launch_tile<BN, kTileK_Grouped, true>(ta, tb, kp, st);
 }
 
