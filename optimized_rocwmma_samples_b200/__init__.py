@@ -10,6 +10,7 @@ from .api import (  # noqa: F401
     Workspace,
     debug_bounded_wait,
     gemm_quant,
+    gemm_quant_host,
     gemm_quant_tensor_scale,
     kernel_moe_smoothquant,
     kernel_smoothquant,

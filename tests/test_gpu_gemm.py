@@ -183,3 +183,24 @@ def test_bounded_wait_reports_timeout(cuda_device):
     st = api.debug_bounded_wait(2000)
     assert st == 4  # B2SQ_ERR_TIMEOUT
     run_case(128, 256, 256)
+
+
+@pytest.mark.parametrize("M,N,K,chunks", [(1000, 512, 256, 3), (4096, 1024, 512, 8), (7, 256, 128, 4)])
+def test_gemm_from_host_buffers(cuda_device, M, N, K, chunks):
+    """gemm_quant_host (pinned host operands and result, chunked and overlapped)
+    equals gemm_quant on device tensors, bit for bit, and reuses its buffers."""
+    from optimized_rocwmma_samples_b200 import api, synth
+
+    dev = cuda_device
+    a = synth.torch_int8_uniform((M, K), dev, 11)
+    w = synth.torch_int8_uniform((N, K), dev, 12)
+    sa, sb = synth.torch_scales(M, dev, 13), synth.torch_scales(N, dev, 14)
+    ref = api.gemm_quant(a, w.t(), sa, sb, out_dtype=torch.bfloat16)
+    h = [t.cpu().pin_memory() for t in (a, w, sa, sb)]
+    h_c = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    bufs = None
+    for _ in range(2):
+        h_c.zero_()
+        bufs = api.gemm_quant_host(*h, h_c, out_dtype=torch.bfloat16, chunks=chunks, buffers=bufs)
+        torch.cuda.synchronize()
+        assert torch.equal(h_c, ref.cpu())
