@@ -351,10 +351,16 @@ def main():
     s_pf = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
     ops_pf = 2.0 * PM * PN * K
     ms_pf = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", False), 10)
+    xq_pf, rs_pf = api.smoothquant(x_pf, s_pf)
+    ms_gm = timed(lambda: layer.ops.gemm(xq_pf, layer.w, rs_pf, layer.sb), 10)
     prefill = {"shape": [PM, K, PN], "shard_cols": n1 - n0,
                "sharded_compute": {"ms": ms_pf, "tops": ops_pf / (ms_pf * 1e-3) / 1e12,
                                    "note": "x replicated, each rank quantises and multiplies its N shard, "
-                                           "output left N-sharded"}}
+                                           "output left N-sharded"},
+               "sharded_gemm": {"ms": ms_gm, "tops": ops_pf / (ms_gm * 1e-3) / 1e12,
+                                "note": "the GEMM alone on each rank's N shard (max over ranks); "
+                                        "scaling = the 1-GPU ms / this"}}
+    del xq_pf, rs_pf
     if world > 1:
         ms_e = timed(lambda: layer.forward(x_pf if rank == 0 else None, s_pf, PM, K, "rank0", True), 5)
         prefill["with_collectives"] = {"ms": ms_e, "tops": ops_pf / (ms_e * 1e-3) / 1e12,

@@ -1105,7 +1105,12 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
         const uint64_t tm2 = (Mk + 255) / 256, tn2 = (Nk + kPairBN - 1) / kPairBN, T2 = tm2 * tn2;
         const uint64_t pairs = P / 2, rounds = (T2 + pairs - 1) / pairs;
         const double loss = (double)(rounds * pairs - T2) / (double)(rounds * pairs);
-        if (T2 >= pairs && loss <= kStreamKMinTailLoss) {
+        // With many rounds a partly idle last round costs less than 1-CTA
+        // tiles would (they run at about 0.7 of a pair's rate, L2-bound);
+        // with few rounds the pairs' fixed costs dominate (measured: 4096^3,
+        // 4 rounds at 13% idle, 12% slower on pairs than on 1-CTA stream-K).
+        const bool many_rounds = rounds >= 8 && loss <= 0.15;
+        if (T2 >= pairs && (loss <= kStreamKMinTailLoss || many_rounds)) {
             s.cta_pair = 1;
             s.tile_n = kPairBN;
             s.tile_k = kPairBK;

@@ -1,4 +1,4 @@
-"""Two GPUs (skipped with fewer): the fused GEMM + all-gather
+"""Two GPUs, and all of them up to eight (skipped with fewer): the fused GEMM + all-gather
 (b2sq_gemm_i8_allgather through ShardedPrefill, peer buffers mapped by CUDA
 IPC, plain NVLink stores from the epilogue) must give every rank the same
 [M, N] output as the single-GPU GEMM and as GEMM + NCCL all-gather, bit for
@@ -61,11 +61,16 @@ def free_port():
         return sk.getsockname()[1]
 
 
-@pytest.mark.timeout(600)
-def test_fused_gemm_allgather_two_gpus():
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
+def worlds():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return sorted({2, min(n, 8)}) if n >= 2 else [2]
+
+
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("world", worlds())
+def test_fused_gemm_allgather_multi_gpu(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
