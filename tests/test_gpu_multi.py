@@ -13,7 +13,9 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(512, 1024, 4096), (300, 2048, 2816), (16, 8192, 4096)]  # (M, K, N); N = 2816: unequal 256-wide shards
+# (M, K, N): N = 2816 gives unequal 256-wide shards; M = 16 the swapped (decode) kernel; 9472 x 1024 at two
+# ranks is 37 x 2 = 74 CTA-pair tiles per shard, so the pair kernel's epilogue does the gathering
+SHAPES = [(512, 1024, 4096), (300, 2048, 2816), (16, 8192, 4096), (9472, 1024, 1024)]
 
 
 def worker(rank, world, port, q):
