@@ -238,6 +238,26 @@ B2SQ_API b2sq_status b2sq_gemm_i8_allgather(uint32_t m, uint32_t n, uint32_t k,
                                   void* workspace, size_t workspace_bytes,
                                   b2sq_stream_t stream);
 
+/*
+ * The same fused GEMM + all-gather through NVSwitch multicast: c_multicast is
+ * an NVLink multicast address (a cuMulticast object every rank bound its
+ * own copy of the [m, N] output buffer to, e.g. torch symmetric memory's
+ * multicast_ptr) and c_local this rank's own mapping of its buffer.  Each
+ * output piece is stored once with multimem.st and the switch writes it to
+ * every rank, so a GPU sends its shard across NVLink once instead of once per
+ * peer.  Requires m > 128, row-major a, n a multiple of 64 and 16-byte
+ * aligned rows; the caller orders the exchange with barriers as above.
+ */
+B2SQ_API b2sq_status b2sq_gemm_i8_allgather_mc(uint32_t m, uint32_t n, uint32_t k,
+                                     const int8_t* a, b2sq_layout la, uint32_t lda,
+                                     const int8_t* b, b2sq_layout lb, uint32_t ldb,
+                                     void* c_local, void* c_multicast, uint32_t col_offset,
+                                     b2sq_dtype c_type, uint32_t ldc,
+                                     const float* scale_a_row, const float* scale_b_col,
+                                     float scale_a, float scale_b,
+                                     void* workspace, size_t workspace_bytes,
+                                     b2sq_stream_t stream);
+
 /* CUDA IPC for the all-gather buffers: export a device pointer (memory from
  * cudaMalloc, any offset inside it) as a 64-byte handle plus offset, open a
  * peer's handle in this process (the returned base + offset is the peer's

@@ -67,6 +67,8 @@ SIGNATURES = {
     "b2sq_gemm_i8_plan": (_i, [_u32, _u32, _u32, _i, _i, _i, _u32, C.POINTER(GemmPlan)]),
     "b2sq_gemm_i8_allgather": (_i, [_u32, _u32, _u32, _vp, _i, _u32, _vp, _i, _u32, _vp, _u32, _u32, _u32, _i, _u32,
                                     _vp, _vp, _f32, _f32, _vp, C.c_size_t, _vp]),
+    "b2sq_gemm_i8_allgather_mc": (_i, [_u32, _u32, _u32, _vp, _i, _u32, _vp, _i, _u32, _vp, _vp, _u32, _i, _u32,
+                                       _vp, _vp, _f32, _f32, _vp, C.c_size_t, _vp]),
     "b2sq_ipc_export": (_i, [_vp, _vp, C.POINTER(C.c_uint64)]),
     "b2sq_ipc_open": (_i, [_vp, C.POINTER(C.c_void_p)]),
     "b2sq_ipc_close": (_i, [_vp]),

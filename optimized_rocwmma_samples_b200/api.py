@@ -308,6 +308,29 @@ def gemm_allgather(a: torch.Tensor, b: torch.Tensor, c_ranks: list, rank: int, c
     _lib.check(st, "b2sq_gemm_i8_allgather")
 
 
+def gemm_allgather_mc(a: torch.Tensor, b: torch.Tensor, c_local: int, c_multicast: int, col_offset: int, ldc: int,
+                      scale_a_row: Optional[torch.Tensor] = None, scale_b_col: Optional[torch.Tensor] = None,
+                      scale_a: float = 1.0, scale_b: float = 1.0, out_dtype: torch.dtype = torch.bfloat16,
+                      workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """gemm_allgather through an NVSwitch multicast mapping (b2sq_gemm_i8_allgather_mc):
+    c_local / c_multicast are the addresses of this rank's [M, ldc] buffer and
+    of its multicast view; each output piece is stored once for all ranks."""
+    if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError("a int8 [M, K] and b int8 [K, N] expected")
+    M, K = a.shape
+    N = b.shape[1]
+    la, lda = _layout_of(a, M, K)
+    lb, ldb = _layout_of(b, K, N)
+    dev = _need_cuda(a, b, scale_a_row, scale_b_col)
+    ws = (workspace or _default_ws).get(dev, workspace_size(M, N, K, la, lb))
+    lib = _lib.load()
+    st = lib.b2sq_gemm_i8_allgather_mc(M, N, K, a.data_ptr(), la, lda, b.data_ptr(), lb, ldb, c_local, c_multicast,
+                                       col_offset, _DTYPE_CODE[out_dtype], ldc, _ptr(scale_a_row), _ptr(scale_b_col),
+                                       float(scale_a), float(scale_b), _ptr(ws), 0 if ws is None else ws.numel(),
+                                       _stream_ptr(stream, dev))
+    _lib.check(st, "b2sq_gemm_i8_allgather_mc")
+
+
 def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
     """(64-byte CUDA IPC handle of the allocation holding t, byte offset of t in it)."""
     _need_cuda(t)

@@ -239,7 +239,7 @@ b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
                          const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
                          const float* scale_a_row, const float* scale_b_col, float scale_a, float scale_b,
                          void* workspace, size_t workspace_bytes, b2sq_stream_t stream, bool a_from_prev_kernel,
-                         void* const* extra_c = nullptr, uint32_t n_extra = 0)
+                         void* const* extra_c = nullptr, uint32_t n_extra = 0, void* mc_c = nullptr)
 {
     b2sq_status st = validate_gemm(m, n, k, a, la, lda, b, lb, ldb, c, c_type, ldc, scale_a_row, scale_b_col);
     if (st != B2SQ_OK || m == 0 || n == 0) return st;
@@ -270,6 +270,7 @@ b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
     p.pdl_dep = a_from_prev_kernel ? (mp.swap ? 2 : 1) : 0;
     p.n_extra = n_extra;
     for (uint32_t d = 0; d < n_extra; ++d) p.extra_c[d] = extra_c[d];
+    p.mc_c = mc_c;
     if (mp.swap) {
         p.a = b;
         p.lda = ldb;
@@ -351,6 +352,30 @@ b2sq_status b2sq_gemm_i8_allgather(uint32_t m, uint32_t n, uint32_t k, const int
         if (r != rank) extra[ne++] = dst[r];
     return gemm_i8_impl(m, n, k, a, la, lda, b, lb, ldb, dst[rank], c_type, ldc, scale_a_row, scale_b_col, scale_a,
                         scale_b, workspace, workspace_bytes, stream, false, extra, ne);
+}
+
+b2sq_status b2sq_gemm_i8_allgather_mc(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la,
+                                      uint32_t lda, const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c_local,
+                                      void* c_multicast, uint32_t col_offset, b2sq_dtype c_type, uint32_t ldc,
+                                      const float* scale_a_row, const float* scale_b_col, float scale_a,
+                                      float scale_b, void* workspace, size_t workspace_bytes, b2sq_stream_t stream)
+{
+    if (!c_local || !c_multicast) return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather_mc: null output pointer");
+    if ((uint64_t)col_offset + n > ldc)
+        return fail(B2SQ_ERR_INVALID_ARG, "gemm_i8_allgather_mc: col_offset + n exceeds ldc");
+    if (m == 0 || n == 0) return ok();
+    // every output store must be a 16-byte vector store (multimem.st has no
+    // narrower form here): no operand swap, whole 32-column chunks, aligned rows
+    if (m <= 128 || la != B2SQ_ROW_MAJOR)
+        return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8_allgather_mc: needs m > 128 and row-major a "
+                                          "(use b2sq_gemm_i8_allgather for decode shapes)");
+    const size_t esz = c_type == B2SQ_I32 ? 4 : 2;
+    uint8_t* dst = static_cast<uint8_t*>(c_local) + (size_t)col_offset * esz;
+    uint8_t* mc = static_cast<uint8_t*>(c_multicast) + (size_t)col_offset * esz;
+    if (n % 64 || !aligned(dst, 16) || !aligned(mc, 16) || ((size_t)ldc * esz) % 16)
+        return fail(B2SQ_ERR_UNSUPPORTED, "gemm_i8_allgather_mc: n a multiple of 64 and 16-byte aligned output rows");
+    return gemm_i8_impl(m, n, k, a, la, lda, b, lb, ldb, dst, c_type, ldc, scale_a_row, scale_b_col, scale_a, scale_b,
+                        workspace, workspace_bytes, stream, false, nullptr, 0, mc);
 }
 
 b2sq_status b2sq_ipc_export(const void* dev_ptr, b2sq_ipc_handle* handle, uint64_t* offset)

@@ -88,6 +88,7 @@ struct KParams {
     int vec_store_ok;
     void* extra_c[kMaxExtraOut];  // further destinations of every store (all-gather)
     uint32_t n_extra;
+    uint8_t* mc_c;  // multicast view of c (all-gather through NVSwitch), or null
     const float* row_scale_vec;
     const float* col_scale_vec;
     float row_scale, col_scale;
@@ -255,6 +256,24 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, int32_t (&acc)[W])
     else tmem_ld_32x32b_x16(taddr, reinterpret_cast<uint32_t(&)[16]>(acc));
 }
 
+// 16 bytes to every rank's buffer at once: a store to an NVSwitch multicast
+// address is replicated by the switch to each GPU bound to the multicast
+// object, so the data crosses this GPU's links once.
+__device__ __forceinline__ void multimem_st16(void* mc_addr, uint4 v)
+{
+    asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "f"(__uint_as_float(v.x)),
+                 "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
+                 : "memory");
+}
+
+// 16-byte store of an output piece at byte offset `off` of c: plain, or
+// through the multicast view.
+__device__ __forceinline__ void st16_out(const KParams& p, void* cbase, size_t off, uint4 v)
+{
+    if (p.mc_c) multimem_st16(p.mc_c + off, v);
+    else *reinterpret_cast<uint4*>(static_cast<uint8_t*>(cbase) + off) = v;
+}
+
 // Stores one dequantised chunk (v, or the raw acc for int32 output) of kernel
 // row `row` into the output buffer at cbase.
 template <uint32_t W>
@@ -268,7 +287,9 @@ __device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t
             if (p.vec_store_ok && col0 + W <= p.Nk) {
 #pragma unroll
                 for (int j = 0; j < (int)W; j += 4)
-                    *reinterpret_cast<int4*>(dst + j) = make_int4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                    st16_out(p, cbase, ((size_t)row * p.ldc + col0 + j) * 4,
+                             make_uint4((uint32_t)acc[j], (uint32_t)acc[j + 1], (uint32_t)acc[j + 2],
+                                        (uint32_t)acc[j + 3]));
             } else {
 #pragma unroll
                 for (int j = 0; j < (int)W; ++j)
@@ -295,7 +316,7 @@ __device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t
                     w = make_uint4(pack_f16(v[j], v[j + 1]), pack_f16(v[j + 2], v[j + 3]),
                                    pack_f16(v[j + 4], v[j + 5]), pack_f16(v[j + 6], v[j + 7]));
                 }
-                *reinterpret_cast<uint4*>(dst + j) = w;
+                st16_out(p, cbase, ((size_t)row * p.ldc + col0 + j) * 2, w);
             }
         } else {
 #pragma unroll
@@ -368,7 +389,7 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
                                            const int32_t (&a1)[W], float rsc, float cs0, float cs1, uint32_t stage)
 {
     if constexpr (W == 32) {
-        if (stage != 0 && p.n_extra > 0 && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
+        if (stage != 0 && (p.n_extra > 0 || p.mc_c) && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
             col0 + 2 * W <= p.Nk) {
             const uint32_t lane = threadIdx.x & 31;
             uint32_t w[32];  // this row's 64 outputs, packed in pairs
@@ -400,9 +421,13 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
                 const uint32_t row_r = __shfl_sync(0xffffffffu, row, r);
                 if (row_r < p.Mk) {
                     const size_t off = (size_t)row_r * ldc_bytes + (size_t)col0 * 2 + c * 16;
-                    *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.c) + off) = val;
-                    for (uint32_t d = 0; d < p.n_extra; ++d)
-                        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.extra_c[d]) + off) = val;
+                    if (p.mc_c) {
+                        multimem_st16(p.mc_c + off, val);
+                    } else {
+                        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.c) + off) = val;
+                        for (uint32_t d = 0; d < p.n_extra; ++d)
+                            *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.extra_c[d]) + off) = val;
+                    }
                 }
             }
             __syncwarp();  // the next pair rewrites the staging area
@@ -1190,6 +1215,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.b_mn_major = p.b_mn_major;
     kp.c = p.c;
     kp.n_extra = p.n_extra;
+    kp.mc_c = static_cast<uint8_t*>(p.mc_c);
     for (uint32_t d = 0; d < p.n_extra && d < kMaxExtraOut; ++d) kp.extra_c[d] = p.extra_c[d];
     kp.ldc = p.ldc;
     kp.c_type = p.c_type;

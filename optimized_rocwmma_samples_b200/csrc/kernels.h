@@ -40,6 +40,10 @@ struct GemmProblem {
     // mapped into this process; plain stores over NVLink).
     void* extra_c[kMaxExtraOut];
     uint32_t n_extra;
+    // Multicast all-gather: when set, every 16-byte output store goes once to
+    // this NVSwitch multicast address (mapping every rank's buffer at the
+    // offset of c) with multimem.st, instead of to c.
+    void* mc_c;
 };
 
 struct GemmSchedule {

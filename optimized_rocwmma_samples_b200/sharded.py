@@ -79,9 +79,43 @@ class PeerOutput:
         self.bases, self.ptrs = [], []
 
 
-def cuda_ops(out_dtype: torch.dtype = torch.bfloat16) -> Ops:
+class MulticastOutput:
+    """A row-major [M, N] output buffer in torch symmetric memory on every
+    rank, with the NVSwitch multicast view that maps all ranks' buffers: one
+    multimem store reaches every rank.  Collective to create; raises if the
+    devices have no multicast support."""
+
+    def __init__(self, m: int, n_total: int, dtype: torch.dtype, device: torch.device, group):
+        import torch.distributed._symmetric_memory as symm
+
+        self.local = symm.empty((m, n_total), dtype=dtype, device=device)
+        self.handle = symm.rendezvous(self.local, group if group is not None else dist.group.WORLD)
+        mc = int(self.handle.multicast_ptr)
+        if mc == 0:
+            raise RuntimeError("no NVSwitch multicast mapping for this buffer")
+        base = int(self.handle.buffer_ptrs[self.handle.rank])
+        self.mc = mc + (self.local.data_ptr() - base)
+
+
+def multicast_supported(device: torch.device) -> bool:
+    try:
+        from torch._C._distributed_c10d import _SymmetricMemory
+        from torch.distributed._symmetric_memory import DeviceType
+
+        return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index or 0))
+    except Exception:  # an older torch, or no symmetric memory support
+        return False
+
+
+def cuda_ops(out_dtype: torch.dtype = torch.bfloat16, gather: str = "auto") -> Ops:
+    """gather: how the fused GEMM + all-gather reaches the other ranks --
+    "multicast" (NVSwitch multimem stores, one copy per output piece),
+    "ipc" (plain stores into every peer's buffer), or "auto" (multicast with
+    three or more ranks, when the devices support it)."""
     from . import api
 
+    if gather not in ("auto", "multicast", "ipc"):
+        raise ValueError("gather must be 'auto', 'multicast' or 'ipc'")
     ws = api.Workspace()
     peers: dict = {}
     flag: dict = {}
@@ -94,14 +128,25 @@ def cuda_ops(out_dtype: torch.dtype = torch.bfloat16) -> Ops:
         dist.all_reduce(flag[dev], group=layer.group)
 
     def gemm_gather(xq, w, sa, sb, n0, n_total, layer):
-        m = xq.shape[0]
-        key = (m, n_total, xq.device)
+        m, n = xq.shape[0], w.shape[0]
+        dev = xq.device
+        # the same choice on every rank (the buffers are created collectively)
+        fits = m > 128 and all((b - a) % 64 == 0 for a, b in layer.shards)
+        # auto: multicast from three ranks on (at two, both paths send the same bytes and the
+        # multicast one also routes this rank's own copy through the switch: 1.66 vs 1.39 ms)
+        use_mc = fits and (gather == "multicast" or (gather == "auto" and layer.world > 2 and multicast_supported(dev)))
+        key = (m, n_total, dev, use_mc)
         if key not in peers:
-            peers[key] = PeerOutput(m, n_total, out_dtype, xq.device, layer.group, layer.world, layer.rank)
+            peers[key] = (MulticastOutput(m, n_total, out_dtype, dev, layer.group) if use_mc else
+                          PeerOutput(m, n_total, out_dtype, dev, layer.group, layer.world, layer.rank))
         po = peers[key]
-        barrier(layer, xq.device)  # every rank is done with the previous contents
-        api.gemm_allgather(xq, w.t(), po.ptrs, layer.rank, n0, n_total, sa, sb, out_dtype=out_dtype, workspace=ws)
-        barrier(layer, xq.device)  # every shard has landed in every buffer
+        barrier(layer, dev)  # every rank is done with the previous contents
+        if use_mc:
+            api.gemm_allgather_mc(xq, w.t(), po.local.data_ptr(), po.mc, n0, n_total, sa, sb, out_dtype=out_dtype,
+                                  workspace=ws)
+        else:
+            api.gemm_allgather(xq, w.t(), po.ptrs, layer.rank, n0, n_total, sa, sb, out_dtype=out_dtype, workspace=ws)
+        barrier(layer, dev)  # every shard has landed in every buffer
         return po.local
 
     return Ops(

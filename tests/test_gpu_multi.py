@@ -1,6 +1,7 @@
 """Two GPUs, and all of them up to eight (skipped with fewer): the fused GEMM + all-gather
-(b2sq_gemm_i8_allgather through ShardedPrefill, peer buffers mapped by CUDA
-IPC, plain NVLink stores from the epilogue) must give every rank the same
+(through ShardedPrefill: b2sq_gemm_i8_allgather with peer buffers mapped by
+CUDA IPC and plain NVLink stores, and b2sq_gemm_i8_allgather_mc with
+NVSwitch multimem stores when the GPUs support multicast) must give every rank the same
 [M, N] output as the single-GPU GEMM and as GEMM + NCCL all-gather, bit for
 bit, over repeated calls that reuse the buffers.  One process per GPU, NCCL."""
 import os
@@ -33,8 +34,11 @@ def worker(rank, world, port, q):
 
         dev = torch.device("cuda", rank)
         res = []
-        for (M, K, N) in SHAPES:
-            ops = cuda_ops(torch.bfloat16)
+        from optimized_rocwmma_samples_b200.sharded import multicast_supported
+
+        modes = ["ipc"] + (["multicast"] if multicast_supported(dev) else [])
+        for (M, K, N), mode in [(shape, mode) for shape in SHAPES for mode in modes]:
+            ops = cuda_ops(torch.bfloat16, gather=mode)
             w = synth.torch_int8_uniform((N, K), dev, 7)  # identical on every rank (seeded)
             sb = synth.torch_scales(N, dev, 8)
             n0, n1 = shard_range(N, world, rank)
@@ -50,9 +54,9 @@ def worker(rank, world, port, q):
                 single = api.gemm_quant(xq, w.t(), rs, sb, out_dtype=torch.bfloat16)
                 torch.cuda.synchronize()
                 res.append((M, K, N, it, bool(torch.equal(fused, single)), bool(torch.equal(nccl, single))))
-        q.put((rank, res, api.last_device_error()))
+        q.put((rank, res, api.last_device_error(), modes))
     except Exception as e:  # report instead of hanging the parent
-        q.put((rank, repr(e), -1))
+        q.put((rank, repr(e), -1, []))
     finally:
         dist.destroy_process_group()
 
@@ -82,7 +86,8 @@ def test_fused_gemm_allgather_multi_gpu(world):
     results = [q.get(timeout=400) for _ in range(world)]
     for p in procs:
         p.join(60)
-    for rank, res, dev_err in results:
+    for rank, res, dev_err, modes in results:
+        print(f"rank {rank}: gather modes {modes}")
         assert isinstance(res, list), f"rank {rank}: {res}"
         assert dev_err == 0
         for M, K, N, it, ok_fused, ok_nccl in res:
