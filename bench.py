@@ -369,25 +369,29 @@ def main():
         # GEMM -> all-gather of the output: NCCL after the GEMM vs fused into the GEMM's epilogue
         ms_g = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", True), 5)
         ms_f = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
-        layer_ipc = ShardedPrefill(w_pf, sb_pf, PN, cuda_ops(torch.bfloat16, gather="ipc"))
-        ms_fi = timed(lambda: layer_ipc.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
         from optimized_rocwmma_samples_b200.sharded import multicast_supported
-        mc = world > 2 and multicast_supported(dev)
+        mc = multicast_supported(dev)
+        ms_fm = None
+        if mc:
+            layer_mc = ShardedPrefill(w_pf, sb_pf, PN, cuda_ops(torch.bfloat16, gather="multicast"))
+            ms_fm = timed(lambda: layer_mc.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
+            del layer_mc
         out_bytes = PM * PN * 2
         prefill["gather_nccl"] = {"ms": ms_g, "tops": ops_pf / (ms_g * 1e-3) / 1e12,
                                   "note": "x replicated, sharded GEMM, then NCCL all-gather into [M, N]"}
         prefill["gather_fused"] = {"ms": ms_f, "tops": ops_pf / (ms_f * 1e-3) / 1e12,
-                                   "path": "multicast" if mc else "ipc",
-                                   "nvlink_bytes_out_per_gpu": out_bytes // world * (1 if mc else world - 1),
-                                   "note": "x replicated, one GEMM whose epilogue gathers the output into every "
-                                           "rank's [M, N] buffer: NVSwitch multimem stores "
-                                           "(b2sq_gemm_i8_allgather_mc) when the GPUs support multicast; "
-                                           "one-element all-reduce barriers before and after"}
-        prefill["gather_fused_ipc"] = {"ms": ms_fi, "tops": ops_pf / (ms_fi * 1e-3) / 1e12,
-                                       "nvlink_bytes_out_per_gpu": out_bytes // world * (world - 1),
-                                       "note": "b2sq_gemm_i8_allgather: the epilogue stores every output tile into "
-                                               "each peer's buffer (CUDA IPC mappings) over NVLink"}
-        del layer_ipc
+                                   "nvlink_bytes_out_per_gpu": out_bytes // world * (world - 1),
+                                   "nvlink_bytes_in_per_gpu": out_bytes // world * (world - 1),
+                                   "note": "x replicated, b2sq_gemm_i8_allgather: one GEMM whose epilogue stores "
+                                           "every output tile into each rank's [M, N] buffer over NVLink (CUDA IPC "
+                                           "mappings); one-element all-reduce barriers before and after"}
+        if ms_fm is not None:
+            prefill["gather_fused_multicast"] = {
+                "ms": ms_fm, "tops": ops_pf / (ms_fm * 1e-3) / 1e12,
+                "nvlink_bytes_out_per_gpu": out_bytes // world,
+                "note": "b2sq_gemm_i8_allgather_mc: each output piece stored once with multimem.st through "
+                        "the NVSwitch multicast mapping (torch symmetric memory); bound like the other by "
+                        "the bytes every GPU receives"}
     del layer, w_pf, x_pf
 
     # ---------------- config 5: MoE, router -> sorting -> MoE smoothquant -> grouped GEMM (replicas)

@@ -110,8 +110,8 @@ def multicast_supported(device: torch.device) -> bool:
 def cuda_ops(out_dtype: torch.dtype = torch.bfloat16, gather: str = "auto") -> Ops:
     """gather: how the fused GEMM + all-gather reaches the other ranks --
     "multicast" (NVSwitch multimem stores, one copy per output piece),
-    "ipc" (plain stores into every peer's buffer), or "auto" (multicast with
-    three or more ranks, when the devices support it)."""
+    "ipc" (plain stores into every peer's buffer), or "auto" (= "ipc", the
+    faster of the two at 2 and at 8 GPUs)."""
     from . import api
 
     if gather not in ("auto", "multicast", "ipc"):
@@ -132,9 +132,10 @@ def cuda_ops(out_dtype: torch.dtype = torch.bfloat16, gather: str = "auto") -> O
         dev = xq.device
         # the same choice on every rank (the buffers are created collectively)
         fits = m > 128 and all((b - a) % 64 == 0 for a, b in layer.shards)
-        # auto: multicast from three ranks on (at two, both paths send the same bytes and the
-        # multicast one also routes this rank's own copy through the switch: 1.66 vs 1.39 ms)
-        use_mc = fits and (gather == "multicast" or (gather == "auto" and layer.world > 2 and multicast_supported(dev)))
+        # auto = ipc: an all-gather is bound by what every GPU must RECEIVE ((world-1)/world of the
+        # output), which multicast does not reduce; measured at 8 GPUs (config 4) 1.42 ms with
+        # peer stores, 1.46 ms with multimem; at 2 GPUs 1.39 vs 1.66 ms
+        use_mc = fits and gather == "multicast" and multicast_supported(dev)
         key = (m, n_total, dev, use_mc)
         if key not in peers:
             peers[key] = (MulticastOutput(m, n_total, out_dtype, dev, layer.group) if use_mc else
