@@ -166,8 +166,9 @@ B2SQ_API b2sq_status b2sq_gemm_i8_no_alloc(uint32_t m, uint32_t n, uint32_t k,
  * sw = scale_w_col ? scale_w_col[j] : scale_w; c f16 or bf16, row-major.
  * Results are identical to the two separate calls.  The GEMM is enqueued
  * with programmatic dependent launch: its prologue and the streaming of the
- * weights overlap the smoothquant kernel, which matters for decode-sized m
- * (the survey's "fuse smoothquant into the GEMM producer" row).  k % 16 == 0.
+ * weights overlap the smoothquant kernel, which matters for decode-sized m,
+ * where the quantisation would otherwise be a separate step of its own.
+ * k % 16 == 0.
  */
 B2SQ_API b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* smooth_scale, float quant_max,
                                               int8_t* xq, float* row_scale, uint32_t m, uint32_t k,
