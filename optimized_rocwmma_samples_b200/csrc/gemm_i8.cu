@@ -213,7 +213,7 @@ __device__ __forceinline__ TileGeom tile_geom(const KParams& p, uint32_t t, cons
     return g;
 }
 
-template <uint32_t BN, uint32_t BK>
+template <uint32_t BN, uint32_t BK, bool G = false>
 struct Smem {
     static constexpr uint32_t ST = num_stages(BN, BK);
     static constexpr uint32_t A_BYTES = kTileM * BK;
@@ -230,7 +230,7 @@ struct Smem {
     // to peer GPUs (all-gather), when the pipeline leaves room for it.
     static constexpr uint32_t epi_off = bar_off + kBarrierBytes;
     static constexpr uint32_t EPI =
-        (bar_off + kBarrierBytes + kEpiStageBytes + 1024 <= kSmemBudget) ? kEpiStageBytes : 0;
+        (G && bar_off + kBarrierBytes + kEpiStageBytes + 1024 <= kSmemBudget) ? kEpiStageBytes : 0;
     static constexpr uint32_t total = bar_off + kBarrierBytes + EPI + 1024;
     static_assert(ST >= 2, "pipeline needs at least two stages");
     static_assert(flag_off + 4 <= bar_off + kBarrierBytes, "barrier area overflow");
@@ -268,15 +268,21 @@ __device__ __forceinline__ void multimem_st16(void* mc_addr, uint4 v)
 
 // 16-byte store of an output piece at byte offset `off` of c: plain, or
 // through the multicast view.
+template <bool G>
 __device__ __forceinline__ void st16_out(const KParams& p, void* cbase, size_t off, uint4 v)
 {
-    if (p.mc_c) multimem_st16(p.mc_c + off, v);
-    else *reinterpret_cast<uint4*>(static_cast<uint8_t*>(cbase) + off) = v;
+    if constexpr (G) {
+        if (p.mc_c) {
+            multimem_st16(p.mc_c + off, v);
+            return;
+        }
+    }
+    *reinterpret_cast<uint4*>(static_cast<uint8_t*>(cbase) + off) = v;
 }
 
 // Stores one dequantised chunk (v, or the raw acc for int32 output) of kernel
 // row `row` into the output buffer at cbase.
-template <uint32_t W>
+template <uint32_t W, bool G>
 __device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t row, uint32_t col0,
                                          const int32_t (&acc)[W], const float (&v)[W])
 {
@@ -287,7 +293,7 @@ __device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t
             if (p.vec_store_ok && col0 + W <= p.Nk) {
 #pragma unroll
                 for (int j = 0; j < (int)W; j += 4)
-                    st16_out(p, cbase, ((size_t)row * p.ldc + col0 + j) * 4,
+                    st16_out<G>(p, cbase, ((size_t)row * p.ldc + col0 + j) * 4,
                              make_uint4((uint32_t)acc[j], (uint32_t)acc[j + 1], (uint32_t)acc[j + 2],
                                         (uint32_t)acc[j + 3]));
             } else {
@@ -316,7 +322,7 @@ __device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t
                     w = make_uint4(pack_f16(v[j], v[j + 1]), pack_f16(v[j + 2], v[j + 3]),
                                    pack_f16(v[j + 4], v[j + 5]), pack_f16(v[j + 6], v[j + 7]));
                 }
-                st16_out(p, cbase, ((size_t)row * p.ldc + col0 + j) * 2, w);
+                st16_out<G>(p, cbase, ((size_t)row * p.ldc + col0 + j) * 2, w);
             }
         } else {
 #pragma unroll
@@ -344,7 +350,9 @@ __device__ __forceinline__ void store_to(const KParams& p, void* cbase, uint32_t
 // csc_lane is the scale of column col0 + (lane % W), so the warp holds the
 // chunk's column scales in one register and shares them by shuffles.
 // Called by all 32 lanes of a warp (the shuffles precede any early exit).
-template <uint32_t W>
+// G: the all-gather build of the epilogue (several destinations or a
+// multicast view); plain GEMMs are compiled without it.
+template <uint32_t W, bool G = false>
 __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&acc)[W],
                                             float rsc, float csc_lane)
 {
@@ -357,9 +365,13 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
         }
     }
     if (row >= p.Mk) return;
-    for (uint32_t d = 0; d <= p.n_extra; ++d) {
-        void* const cbase = d == 0 ? p.c : p.extra_c[d - 1];
-        store_to(p, cbase, row, col0, acc, v);
+    if constexpr (G) {
+        for (uint32_t d = 0; d <= p.n_extra; ++d) {
+            void* const cbase = d == 0 ? p.c : p.extra_c[d - 1];
+            store_to<W, G>(p, cbase, row, col0, acc, v);
+        }
+    } else {
+        store_to<W, G>(p, p.c, row, col0, acc, v);
     }
 }
 
@@ -384,11 +396,11 @@ __device__ __forceinline__ uint4 lds128_epi(uint32_t addr)
 // runs per instruction (measured on B200: 16-byte runs reach a quarter of
 // it), while local stores are combined in L2 either way.  Same values as
 // store_chunk in every case.
-template <uint32_t W>
+template <uint32_t W, bool G>
 __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&a0)[W],
                                            const int32_t (&a1)[W], float rsc, float cs0, float cs1, uint32_t stage)
 {
-    if constexpr (W == 32) {
+    if constexpr (W == 32 && G) {
         if (stage != 0 && (p.n_extra > 0 || p.mc_c) && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
             col0 + 2 * W <= p.Nk) {
             const uint32_t lane = threadIdx.x & 31;
@@ -434,16 +446,16 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
             return;
         }
     }
-    store_chunk<W>(p, row, col0, a0, rsc, cs0);
-    store_chunk<W>(p, row, col0 + W, a1, rsc, cs1);
+    store_chunk<W, G>(p, row, col0, a0, rsc, cs0);
+    store_chunk<W, G>(p, row, col0 + W, a1, rsc, cs1);
 }
 
-template <uint32_t BN, uint32_t BK, bool kGrouped>
+template <uint32_t BN, uint32_t BK, bool kGrouped, bool G = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p,
                    uint64_t wait_limit_ns)
 {
-    using L = Smem<BN, BK>;
+    using L = Smem<BN, BK, G>;
     constexpr uint32_t ST = L::ST;
     constexpr uint32_t TMEM_COLS = tmem_cols(BN);
     constexpr uint32_t CW = BN < 32 ? BN : 32;  // columns per tcgen05.ld
@@ -688,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
-                    store_chunk<CW>(p, row, tn_col0, acc, rsc, csv[0]);
+                    store_chunk<CW, G>(p, row, tn_col0, acc, rsc, csv[0]);
                 } else {
                     // Two chunks per TMEM round trip.
 #pragma unroll
@@ -702,7 +714,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __syncwarp();
                             if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
                         }
-                        store_pair<CW>(p, row, tn_col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
+                        store_pair<CW, G>(p, row, tn_col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
                     }
                 }
             } else {
@@ -757,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (uint32_t j = 0; j < CW; ++j) acc[j] += __ldcg(src + (size_t)(ch * CW + j) * kTileM + row_local);
                         }
-                        store_chunk<CW>(p, row, tn_col0 + ch * CW, acc, rsc, csv[ch]);
+                        store_chunk<CW, G>(p, row, tn_col0 + ch * CW, acc, rsc, csv[ch]);
                     }
                 }
             }
@@ -798,7 +810,8 @@ constexpr uint32_t kPairSB = 2 * kPairHalfBytes;            // A half + B half p
 constexpr uint32_t kPairST = 6;
 constexpr uint32_t kPairBarOff = kPairST * kPairSB;
 constexpr uint32_t kPairEpiOff = kPairBarOff + kBarrierBytes;
-constexpr uint32_t kPairSmem = kPairBarOff + kBarrierBytes + kEpiStageBytes + 1024;
+constexpr uint32_t pair_smem(bool gather) { return kPairBarOff + kBarrierBytes + (gather ? kEpiStageBytes : 0) + 1024; }
+constexpr uint32_t kPairSmem = pair_smem(true);
 static_assert(kPairSmem <= kSmemBudget, "pair kernel shared memory overflow");
 
 // One pair tile: 256 rows from a_row (rows from row_end on are not stored),
@@ -842,7 +855,7 @@ __device__ __forceinline__ PairTile pair_tile(const KParams& p, uint32_t t, cons
     return g;
 }
 
-template <bool kGrouped>
+template <bool kGrouped, bool G = false>
 __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const KParams p, uint64_t wait_limit_ns)
@@ -1002,7 +1015,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
                 }
-                store_pair<CW>(p, row, tg.col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
+                store_pair<CW, G>(p, row, tg.col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
             }
         }
     }
@@ -1066,10 +1079,10 @@ bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint3
     return r == CUDA_SUCCESS;
 }
 
-template <uint32_t BN, uint32_t BK, bool kGrouped = false>
+template <uint32_t BN, uint32_t BK, bool kGrouped = false, bool G = false>
 cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
-    using L = Smem<BN, BK>;
+    using L = Smem<BN, BK, G>;
     // The shared-memory opt-in is a per-device function attribute.
     static std::atomic<uint64_t> done_mask{0};
     int dev = 0;
@@ -1077,7 +1090,7 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  L::total);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
@@ -1093,13 +1106,13 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped>, ta, tb, kp, (uint64_t)kWaitLimitNs);
+        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped, G>, ta, tb, kp, (uint64_t)kWaitLimitNs);
     }
-    gemm_i8_kernel<BN, BK, kGrouped><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_kernel<BN, BK, kGrouped, G><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
-template <bool kGrouped>
+template <bool kGrouped, bool G = false>
 cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
     static std::atomic<uint64_t> done_mask{0};
@@ -1108,11 +1121,12 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 pair_smem(G));
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_pair_kernel<kGrouped><<<kp.ctas, kThreads, kPairSmem, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_pair_kernel<kGrouped, G><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -1233,7 +1247,20 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.raster_group = B2SQ_RASTER_GROUP;
     kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
-    if (s.cta_pair) return launch_pair<false>(ta, tb, kp, st);
+    // The all-gather epilogue (extra destinations / multicast) is a separate
+    // build of each kernel, so plain GEMMs carry none of its code.
+    const bool gather = p.n_extra > 0 || p.mc_c != nullptr;
+    if (s.cta_pair) return gather ? launch_pair<false, true>(ta, tb, kp, st) : launch_pair<false>(ta, tb, kp, st);
+    if (gather) {
+        switch (bn) {
+            case 16: return launch_tile<16, tile_k_for(16), false, true>(ta, tb, kp, st);
+            case 32: return launch_tile<32, tile_k_for(32), false, true>(ta, tb, kp, st);
+            case 64: return launch_tile<64, tile_k_for(64), false, true>(ta, tb, kp, st);
+            case 128: return launch_tile<128, tile_k_for(128), false, true>(ta, tb, kp, st);
+            case 256: return launch_tile<256, tile_k_for(256), false, true>(ta, tb, kp, st);
+            default: break;
+        }
+    }
     switch (bn) {
         case 16: return launch_tile<16, tile_k_for(16)>(ta, tb, kp, st);
         case 32: return launch_tile<32, tile_k_for(32)>(ta, tb, kp, st);
