@@ -366,6 +366,21 @@ __device__ __forceinline__ void store_chunk(const KParams& p, uint32_t row, uint
     }
     if (row >= p.Mk) return;
     if constexpr (G) {
+        if (p.c_type != 2 && !p.transpose_out && p.vec_store_ok && col0 + W <= p.Nk) {
+            // pack once, then the same 16-byte pieces to every destination
+            uint32_t pk[W / 2];
+#pragma unroll
+            for (int j = 0; j < (int)W; j += 2) pk[j / 2] = p.c_type == 1 ? pack_bf16(v[j], v[j + 1]) : pack_f16(v[j], v[j + 1]);
+            const size_t off = ((size_t)row * p.ldc + col0) * 2;
+            for (uint32_t d = 0; d <= p.n_extra; ++d) {
+                void* const cbase = d == 0 ? p.c : p.extra_c[d - 1];
+#pragma unroll
+                for (int j = 0; j < (int)W / 8; ++j)
+                    st16_out<G>(p, cbase, off + (size_t)j * 16,
+                                make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]));
+            }
+            return;
+        }
         for (uint32_t d = 0; d <= p.n_extra; ++d) {
             void* const cbase = d == 0 ? p.c : p.extra_c[d - 1];
             store_to<W, G>(p, cbase, row, col0, acc, v);
@@ -404,26 +419,25 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
         if (stage != 0 && (p.n_extra > 0 || p.mc_c) && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
             col0 + 2 * W <= p.Nk) {
             const uint32_t lane = threadIdx.x & 31;
-            uint32_t w[32];  // this row's 64 outputs, packed in pairs
+            // row-major [32 rows][128 B], 16-byte pieces XOR-swizzled by row (conflict-free both
+            // ways); pieces 0-3 from the first chunk, 4-7 from the second, each written as soon
+            // as it is packed
+            auto stage_chunk = [&](const int32_t (&acc)[W], float cs, uint32_t piece0) {
+                uint32_t w[16];  // 32 outputs packed in pairs
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float c0 = __shfl_sync(0xffffffffu, cs0, j), c1 = __shfl_sync(0xffffffffu, cs0, j + 1);
-                const float v0 = __fmul_rn(__int2float_rn(a0[j]), __fmul_rn(rsc, c0));
-                const float v1 = __fmul_rn(__int2float_rn(a0[j + 1]), __fmul_rn(rsc, c1));
-                w[j / 2] = p.c_type == 1 ? pack_bf16(v0, v1) : pack_f16(v0, v1);
-            }
+                for (int j = 0; j < 32; j += 2) {
+                    const float c0 = __shfl_sync(0xffffffffu, cs, j), c1 = __shfl_sync(0xffffffffu, cs, j + 1);
+                    const float v0 = __fmul_rn(__int2float_rn(acc[j]), __fmul_rn(rsc, c0));
+                    const float v1 = __fmul_rn(__int2float_rn(acc[j + 1]), __fmul_rn(rsc, c1));
+                    w[j / 2] = p.c_type == 1 ? pack_bf16(v0, v1) : pack_f16(v0, v1);
+                }
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float c0 = __shfl_sync(0xffffffffu, cs1, j), c1 = __shfl_sync(0xffffffffu, cs1, j + 1);
-                const float v0 = __fmul_rn(__int2float_rn(a1[j]), __fmul_rn(rsc, c0));
-                const float v1 = __fmul_rn(__int2float_rn(a1[j + 1]), __fmul_rn(rsc, c1));
-                w[16 + j / 2] = p.c_type == 1 ? pack_bf16(v0, v1) : pack_f16(v0, v1);
-            }
-            // row-major [32 rows][128 B], 16-byte pieces XOR-swizzled by row (conflict-free both ways)
-#pragma unroll
-            for (uint32_t c = 0; c < 8; ++c)
-                sts128(stage + lane * 128 + ((c ^ (lane & 7)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
-                       w[4 * c + 3]);
+                for (uint32_t c = 0; c < 4; ++c)
+                    sts128(stage + lane * 128 + (((piece0 + c) ^ (lane & 7)) << 4), w[4 * c], w[4 * c + 1],
+                           w[4 * c + 2], w[4 * c + 3]);
+            };
+            stage_chunk(a0, cs0, 0);
+            stage_chunk(a1, cs1, 4);
             __syncwarp();
             const size_t ldc_bytes = (size_t)p.ldc * 2;
 #pragma unroll
