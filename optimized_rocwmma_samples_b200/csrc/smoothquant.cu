@@ -704,9 +704,9 @@ unsigned generic_grid(uint64_t rows)
 // ------------------------------------------------------------- streaming path
 namespace {
 
-// Inputs of at least this many elements take the streaming kernels.
-// (crossover measured on B200: at 3328 x 4096 the register-resident kernel is
-// faster, from 3328 x 8192 up the streaming one)
+// Inputs of at least this many elements (rows of 8192+) take the streaming
+// kernel (crossover measured on B200: at 3328 x 4096 the register-resident
+// kernel is faster, from 3328 x 8192 up the streaming one).
 constexpr uint64_t kTmaMinElems = 1ull << 24;
 constexpr uint32_t kTmaRingBytes = 110 * 1024;   // rows up to half of this take the streaming kernel
 constexpr uint32_t kTmaRingTarget = 52 * 1024;   // input ring per CTA
@@ -776,7 +776,12 @@ bool use_tma(uint64_t rows, uint32_t row_elems, uint32_t& vpt)
 {
     const uint32_t nvec = row_elems / 8;
     vpt = (nvec + kTmaConsumers - 1) / kTmaConsumers;
-    return rows * row_elems >= kTmaMinElems && vpt >= 1 && vpt <= 8 && row_elems * 2 <= kTmaRingBytes / 2;
+    // Rows of 8192+ elements stream from 2^24 elements on; 4096-element rows
+    // only from 2^27 (16384 x 4096: register-resident 47 us vs 51 streaming;
+    // 65536 x 4096: 190 vs 178); shorter rows never (32768 x 2048: 45 vs 70).
+    const uint64_t elems = rows * row_elems;
+    const bool big = row_elems >= 8192 ? elems >= kTmaMinElems : row_elems >= 4096 && elems >= (kTmaMinElems << 3);
+    return big && vpt >= 1 && vpt <= 8 && row_elems * 2 <= kTmaRingBytes / 2;
 }
 
 }  // namespace

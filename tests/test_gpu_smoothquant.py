@@ -128,11 +128,12 @@ def test_special_values_and_qmax(cuda_device, qmax):
 
 @pytest.mark.parametrize("qmax", [127.0, 100.5])
 def test_special_values_streaming_path(cuda_device, qmax):
-    """Inputs of >= 16M elements take the TMA-staged kernel; rows with NaN, +-inf,
-    overflow to inf after smoothing, or all-subnormal values take its exact
-    (clamped) branch, ordinary rows its fast branch.  All bit-exact."""
+    """Rows of 8192+ elements in inputs of >= 2^24 elements take the TMA-staged
+    kernel; rows with NaN, +-inf, overflow to inf after smoothing, or
+    all-subnormal values take its exact (clamped) branch, ordinary rows its
+    fast branch.  All bit-exact."""
     rng = np.random.default_rng(77)
-    M, N = 17000, 1024  # >= 2^24 elements, also with N = 1000
+    M, N = 2050, 8200  # 2050 x 8192 >= 2^24 elements; N = 8200: rows not a multiple of 16 bytes
     x = synth.activations_np(rng, M, N, 8, 20.0)
     s = synth.smooth_np(rng, N)
     x[10, 5] = np.nan
@@ -144,5 +145,5 @@ def test_special_values_streaming_path(cuda_device, qmax):
     s[3] = 1e38                       # x[15,3] * s[3] overflows fp32 -> inf
     x[16, 9] = np.nan
     x[16, 10] = np.inf
-    check_sq(x, s, qmax)
-    check_sq(x[:, :1000].copy(), s[:1000].copy(), qmax)  # row bytes not a multiple of 16: direct stores
+    check_sq(x[:, :8192].copy(), s[:8192].copy(), qmax)  # whole-row bulk stores
+    check_sq(x, s, qmax)  # row bytes not a multiple of 16: direct stores
