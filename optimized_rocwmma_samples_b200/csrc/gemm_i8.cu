@@ -952,8 +952,12 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     const uint32_t fb_leader = mapa_shared(fb, 0);
                     const uint32_t sa = sbase + stage * kPairSB;
                     const int32_t kc = (int32_t)(kb * kPairBK);
-                    tma_load_2d_pair(sa, &tmA, fb_leader, kc, a_row);
-                    tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, kc, b_row);
+                    // K-major: box {128 k, 128 rows}; MN-major: box {128 rows, 128 k} (one
+                    // 128-byte swizzle atom along M or N: each CTA holds 128 of them)
+                    if (p.a_mn_major) tma_load_2d_pair(sa, &tmA, fb_leader, a_row, kc);
+                    else tma_load_2d_pair(sa, &tmA, fb_leader, kc, a_row);
+                    if (p.b_mn_major) tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, b_row, kc);
+                    else tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, kc, b_row);
                     if (++stage == ST) stage = 0, phase ^= 1;
                 }
             }
@@ -962,7 +966,10 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc = idesc_i8(256, kPairBN, 0, 0);
+            const uint32_t idesc = idesc_i8(256, kPairBN, p.a_mn_major, p.b_mn_major);
+            // K-major: 32-byte steps inside the swizzled rows; MN-major: 32 k rows of 128 bytes
+            const uint32_t a_step = p.a_mn_major ? 32 * 128 : 32, b_step = p.b_mn_major ? 32 * 128 : 32;
+            const uint32_t a_lbo = p.a_mn_major ? 128 * kPairBK : 16, b_lbo = p.b_mn_major ? 128 * kPairBK : 16;
             uint32_t stage = 0, phase = 0, uidx = 0;
             bool ok = true;
             for (uint32_t t = pair; ok && t < T; t += npairs, ++uidx) {
@@ -982,8 +989,8 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     const uint32_t sa = sbase + stage * kPairSB;
 #pragma unroll
                     for (uint32_t kk = 0; kk < kPairBK / 32; ++kk) {
-                        const uint64_t ad = umma_desc_sw128(sa + kk * 32, 16, 1024);
-                        const uint64_t bd = umma_desc_sw128(sa + kPairHalfBytes + kk * 32, 16, 1024);
+                        const uint64_t ad = umma_desc_sw128(sa + kk * a_step, a_lbo, 1024);
+                        const uint64_t bd = umma_desc_sw128(sa + kPairHalfBytes + kk * b_step, b_lbo, 1024);
                         mma_i8_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                     }
                     mma_commit_pair(empty_bar + 8 * stage, 0x3);
@@ -1152,29 +1159,25 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
     s = GemmSchedule{};
     const uint32_t P = num_sms ? num_sms : 148;
 #ifndef B2SQ_DISABLE_PAIR
-    // CTA-pair 256 x 256 tiles for large K-major problems whose whole-tile
-    // rounds leave at most kStreamKMinTailLoss of the pairs idle.
-    if (!a_mn_major && !b_mn_major && Mk >= 256 && Nk >= 256 && P >= 2) {
+    // CTA-pair 256 x 256 tiles for every problem of at least 256 x 256 (either
+    // operand K-major or MN-major): a 1-CTA 128 x 256 tile streams 1.5x the operand bytes per MMA and
+    // is L2-bound (ncu: 57-60% against 84% tensor utilisation), so pairs win
+    // even when most of their last round is idle (measured on B200, in us,
+    // pairs vs 1-CTA stream-K: 4096^3 57.9 vs 82.4; 512 x 8192 x 8192 37.3 vs
+    // 76.3; 1280 x 4096 x 8192, 46% of the last round idle, 53.8 vs 57.8).
+    if (Mk >= 256 && Nk >= 256 && P >= 2) {
         const uint64_t tm2 = (Mk + 255) / 256, tn2 = (Nk + kPairBN - 1) / kPairBN, T2 = tm2 * tn2;
-        const uint64_t pairs = P / 2, rounds = (T2 + pairs - 1) / pairs;
-        const double loss = (double)(rounds * pairs - T2) / (double)(rounds * pairs);
-        // With many rounds a partly idle last round costs less than 1-CTA
-        // tiles would (they run at about 0.7 of a pair's rate, L2-bound);
-        // with few rounds the pairs' fixed costs dominate (measured: 4096^3,
-        // 4 rounds at 13% idle, 12% slower on pairs than on 1-CTA stream-K).
-        const bool many_rounds = rounds >= 8 && loss <= 0.15;
-        if (T2 >= pairs && (loss <= kStreamKMinTailLoss || many_rounds)) {
-            s.cta_pair = 1;
-            s.tile_n = kPairBN;
-            s.tile_k = kPairBK;
-            s.stages = kPairST;
-            s.tiles_m = (uint32_t)tm2;
-            s.tiles_n = (uint32_t)tn2;
-            s.k_blocks = (K + kPairBK - 1) / kPairBK;
-            s.dp_tiles = (uint32_t)T2;
-            s.ctas = (uint32_t)(2 * pairs);
-            return;
-        }
+        const uint64_t pairs = P / 2;
+        s.cta_pair = 1;
+        s.tile_n = kPairBN;
+        s.tile_k = kPairBK;
+        s.stages = kPairST;
+        s.tiles_m = (uint32_t)tm2;
+        s.tiles_n = (uint32_t)tn2;
+        s.k_blocks = (K + kPairBK - 1) / kPairBK;
+        s.dp_tiles = (uint32_t)T2;
+        s.ctas = (uint32_t)(2 * (T2 < pairs ? T2 : pairs));
+        return;
     }
 #endif
     uint32_t bn = 16;

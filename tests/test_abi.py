@@ -100,7 +100,7 @@ def simulate_units(pl):
 
 
 @pytest.mark.parametrize("m,n,k", [(8192, 8192, 8192), (16, 28672, 8192), (64, 28672, 8192),
-                                   (16384, 28672, 8192), (19 * 128, 20 * 256, 1024), (1, 16, 16),
+                                   (16384, 28672, 8192), (19 * 128, 20 * 256, 1024), (1, 16, 16), (512, 8192, 8192), (200, 8192, 1024),
                                    (3000, 3000, 3000), (128, 128, 128 * 1000)])
 @pytest.mark.parametrize("sk", [True, False])
 def test_schedule_covers_each_kblock_once(m, n, k, sk):
@@ -127,10 +127,15 @@ def test_plan_choices():
     # CTA pairs: 1024 tiles of 256 x 256 over 74 pairs, 14 rounds, 1.2% idle
     assert p.cta_pair == 1 and p.swap_ab == 0 and p.tile_m == 256 and p.tile_n == 256
     assert p.tiles_m * p.tiles_n == 1024 and p.dp_tiles == 1024 and p.sk_iters == 0 and p.ctas == 148
-    p = api.plan(8192, 8192, 8192, api.COL_MAJOR, api.COL_MAJOR, num_sms=148)  # MN-major A: one CTA per tile
-    assert p.cta_pair == 0 and p.tile_n == 256 and p.dp_tiles == 2048 and p.sk_iters == 0
+    p = api.plan(8192, 8192, 8192, api.COL_MAJOR, api.ROW_MAJOR, num_sms=148)  # the reference's layouts: pairs too
+    assert p.cta_pair == 1 and p.tile_n == 256 and p.dp_tiles == 1024 and p.sk_iters == 0
     p = api.plan(19 * 128, 20 * 256, 1024, num_sms=148)
-    assert p.dp_tiles == 0 and p.sk_iters == 380 * p.k_blocks  # 2.6 rounds: all stream-K
+    assert p.cta_pair == 1 and p.dp_tiles == 10 * 20  # CTA pairs even with 2.7 rounds (L2-bound 1-CTA tiles lose)
+    p = api.plan(512, 8192, 8192, num_sms=148)
+    assert p.cta_pair == 1 and p.dp_tiles == 64 and p.ctas == 128  # fewer tiles than pairs: one tile per pair
+    p = api.plan(200, 8192, 1024, num_sms=148)
+    # fewer rows than a pair tile, not skinny enough to swap: 1-CTA 128 x 256 tiles, all stream-K
+    assert p.cta_pair == 0 and p.tile_n == 256 and p.dp_tiles == 0 and p.sk_iters == 64 * p.k_blocks
     p = api.plan(8192, 8192, 8192, api.ROW_MAJOR, api.ROW_MAJOR, num_sms=148)
     assert p.tile_n in (128, 256)
 

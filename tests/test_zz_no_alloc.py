@@ -65,12 +65,13 @@ def test_no_alloc_matches_workspace_entry_point(cuda_device, M, N, K):
 
 
 def test_no_alloc_rejects_oversized_scratch(cuda_device):
-    # 2048^3: 64 tiles of 128 x 256 over 148 SMs, all stream-K: ~39 MiB of scratch (> 24 MiB)
+    # 200 x 8192 x 2048: fewer rows than a CTA-pair tile, too many to swap the operands:
+    # 1-CTA 128 x 256 tiles, 64 of them over 148 SMs, all stream-K: ~39 MiB of scratch (> 24 MiB)
     dev = cuda_device
-    a = synth.torch_int8_uniform((2048, 2048), dev, 1)
-    w = synth.torch_int8_uniform((2048, 2048), dev, 2)
-    sa, sb = synth.torch_scales(2048, dev, 3), synth.torch_scales(2048, dev, 4)
-    need = api.workspace_size(2048, 2048, 2048)
+    a = synth.torch_int8_uniform((200, 2048), dev, 1)
+    w = synth.torch_int8_uniform((8192, 2048), dev, 2)
+    sa, sb = synth.torch_scales(200, dev, 3), synth.torch_scales(8192, dev, 4)
+    need = api.workspace_size(200, 8192, 2048)
     assert need > 24 << 20
     st, _ = no_alloc(a, w, sa, sb, torch.float16)
     assert st == _lib.B2SQ_ERR_UNSUPPORTED
