@@ -36,3 +36,43 @@ def test_fused_matches_separate_and_oracle(cuda_device, M, K, N, dt):
     ref = O.dequant(acc, r0[rows], sb.cpu().numpy(), out_dtype="f16" if dt == torch.float16 else "bf16")
     assert np.array_equal(c[rows].view(torch.int16).cpu().numpy().view(np.uint16), ref)
     assert api.last_device_error() == 0
+
+
+def test_fused_decode_replays_in_a_cuda_graph(cuda_device):
+    """The fused decode call (smoothquant -> GEMM chained by programmatic
+    dependent launch) captures into a CUDA graph; replays with new input
+    values in the captured buffers give the results of direct calls."""
+    from optimized_rocwmma_samples_b200 import api, synth
+
+    dev = cuda_device
+    M, K, N = 16, 4096, 8192
+    w = synth.torch_int8_uniform((N, K), dev, 41)
+    sb = synth.torch_scales(N, dev, 42)
+    s = torch.empty((K,), device=dev).uniform_(0.5, 2.0)
+    x = torch.empty((M, K), dtype=torch.float16, device=dev)
+    y = torch.empty((M, K), dtype=torch.int8, device=dev)
+    r = torch.empty((M,), dtype=torch.float32, device=dev)
+    o = torch.empty((M, N), dtype=torch.float16, device=dev)
+    ws = api.Workspace()
+
+    def step():
+        api.smoothquant_gemm(x, s, w, sb, out_dtype=torch.float16, xq=y, row_scale=r, c=o, workspace=ws)
+
+    x.copy_(torch.randn((M, K), device=dev).to(torch.float16))
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        step()  # first call outside capture: one-time attribute setup
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    for seed in range(3):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        x.copy_((torch.randn((M, K), generator=g, device=dev) * 2).to(torch.float16))
+        graph.replay()
+        torch.cuda.synchronize()
+        got = o.clone()
+        ref, _, _ = api.smoothquant_gemm(x, s, w, sb, out_dtype=torch.float16, workspace=ws)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref)
