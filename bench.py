@@ -375,6 +375,7 @@ def main():
         if mc:
             layer_mc = ShardedPrefill(w_pf, sb_pf, PN, cuda_ops(torch.bfloat16, gather="multicast"))
             ms_fm = timed(lambda: layer_mc.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
+            layer_mc.ops.close()
             del layer_mc
         out_bytes = PM * PN * 2
         prefill["gather_nccl"] = {"ms": ms_g, "tops": ops_pf / (ms_g * 1e-3) / 1e12,
@@ -392,6 +393,7 @@ def main():
                 "note": "b2sq_gemm_i8_allgather_mc: each output piece stored once with multimem.st through "
                         "the NVSwitch multicast mapping (torch symmetric memory); bound like the other by "
                         "the bytes every GPU receives"}
+    layer.ops.close()
     del layer, w_pf, x_pf
 
     # ---------------- config 5: MoE, router -> sorting -> MoE smoothquant -> grouped GEMM (replicas)

@@ -47,6 +47,7 @@ class Ops:
     smoothquant: Callable
     gemm: Callable
     gemm_gather: Optional[Callable] = None
+    close: Callable = lambda: None  # releases buffers / peer mappings the steps created
 
 
 class PeerOutput:
@@ -150,10 +151,18 @@ def cuda_ops(out_dtype: torch.dtype = torch.bfloat16, gather: str = "auto") -> O
         barrier(layer, dev)  # every shard has landed in every buffer
         return po.local
 
+    def close():
+        torch.cuda.synchronize()
+        for po in peers.values():
+            if isinstance(po, PeerOutput):
+                po.close()
+        peers.clear()
+
     return Ops(
         smoothquant=lambda x, s: api.smoothquant(x, s),
         gemm=lambda xq, w, sa, sb: api.gemm_quant(xq, w.t(), sa, sb, out_dtype=out_dtype, workspace=ws),
         gemm_gather=gemm_gather,
+        close=close,
     )
 
 

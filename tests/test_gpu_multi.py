@@ -54,6 +54,7 @@ def worker(rank, world, port, q):
                 single = api.gemm_quant(xq, w.t(), rs, sb, out_dtype=torch.bfloat16)
                 torch.cuda.synchronize()
                 res.append((M, K, N, it, bool(torch.equal(fused, single)), bool(torch.equal(nccl, single))))
+            ops.close()  # unmaps the peers' buffers (all ranks are past their last exchange)
         q.put((rank, res, api.last_device_error(), modes))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e), -1, []))
