@@ -230,7 +230,7 @@ struct Smem {
     // to peer GPUs (all-gather), when the pipeline leaves room for it.
     static constexpr uint32_t epi_off = bar_off + kBarrierBytes;
     static constexpr uint32_t EPI =
-        (G && bar_off + kBarrierBytes + kEpiStageBytes + 1024 <= kSmemBudget) ? kEpiStageBytes : 0;
+        (bar_off + kBarrierBytes + kEpiStageBytes + 1024 <= kSmemBudget) ? kEpiStageBytes : 0;
     static constexpr uint32_t total = bar_off + kBarrierBytes + EPI + 1024;
     static_assert(ST >= 2, "pipeline needs at least two stages");
     static_assert(flag_off + 4 <= bar_off + kBarrierBytes, "barrier area overflow");
@@ -403,20 +403,29 @@ __device__ __forceinline__ uint4 lds128_epi(uint32_t addr)
     return v;
 }
 
-// Two consecutive W-column chunks of the warp's 32 rows.  With extra (peer)
-// destinations, a 16-bit output and room to stage (stage = this warp's 4 KiB
-// of shared memory, 0 if none), the 32 x 64 values are re-shaped through
-// shared memory so that every store instruction writes 4 rows x 128
-// contiguous bytes: NVLink moves peer stores at full rate only from 128-byte
-// runs per instruction (measured on B200: 16-byte runs reach a quarter of
-// it), while local stores are combined in L2 either way.  Same values as
-// store_chunk in every case.
+// Two consecutive W-column chunks of the warp's 32 rows.  With a 16-bit
+// output and room to stage (stage = this warp's 4 KiB of shared memory, 0 if
+// none), the 32 x 64 values are re-shaped through shared memory so that
+// every store instruction writes 4 rows x 128 contiguous bytes instead of 32
+// rows x 16 bytes: 8x fewer L2 requests (8192^2 x 2048: 117 -> 105 us), and
+// NVLink moves peer stores (the all-gather build) at full rate only from
+// 128-byte runs (measured: 16-byte runs reach a quarter of it).  Same values
+// as store_chunk in every case.
+// Output store of the staged path, marked evict-first (.cs): the output is
+// written once and not re-read by this kernel, so it should not push operand
+// tiles other CTAs still need out of L2 (measured 1-2% at 8192^2 x 2048).
+__device__ __forceinline__ void st_out16(void* p, uint4 v)
+{
+    asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 template <uint32_t W, bool G>
 __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&a0)[W],
                                            const int32_t (&a1)[W], float rsc, float cs0, float cs1, uint32_t stage)
 {
-    if constexpr (W == 32 && G) {
-        if (stage != 0 && (p.n_extra > 0 || p.mc_c) && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
+    if constexpr (W == 32) {
+        if (stage != 0 && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
             col0 + 2 * W <= p.Nk) {
             const uint32_t lane = threadIdx.x & 31;
             // row-major [32 rows][128 B], 16-byte pieces XOR-swizzled by row (conflict-free both
@@ -447,12 +456,16 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
                 const uint32_t row_r = __shfl_sync(0xffffffffu, row, r);
                 if (row_r < p.Mk) {
                     const size_t off = (size_t)row_r * ldc_bytes + (size_t)col0 * 2 + c * 16;
-                    if (p.mc_c) {
-                        multimem_st16(p.mc_c + off, val);
+                    if constexpr (G) {
+                        if (p.mc_c) {
+                            multimem_st16(p.mc_c + off, val);
+                        } else {
+                            *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.c) + off) = val;
+                            for (uint32_t d = 0; d < p.n_extra; ++d)
+                                *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.extra_c[d]) + off) = val;
+                        }
                     } else {
-                        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.c) + off) = val;
-                        for (uint32_t d = 0; d < p.n_extra; ++d)
-                            *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.extra_c[d]) + off) = val;
+                        st_out16(static_cast<uint8_t*>(p.c) + off, val);
                     }
                 }
             }
@@ -824,7 +837,7 @@ constexpr uint32_t kPairSB = 2 * kPairHalfBytes;            // A half + B half p
 constexpr uint32_t kPairST = 6;
 constexpr uint32_t kPairBarOff = kPairST * kPairSB;
 constexpr uint32_t kPairEpiOff = kPairBarOff + kBarrierBytes;
-constexpr uint32_t pair_smem(bool gather) { return kPairBarOff + kBarrierBytes + (gather ? kEpiStageBytes : 0) + 1024; }
+constexpr uint32_t pair_smem(bool) { return kPairBarOff + kBarrierBytes + kEpiStageBytes + 1024; }
 constexpr uint32_t kPairSmem = pair_smem(true);
 static_assert(kPairSmem <= kSmemBudget, "pair kernel shared memory overflow");
 
