@@ -84,7 +84,8 @@ def test_skinny_m_swap(cuda_device, M, N, K):
     run_case(M, N, K, "row", "col", out="f16")
 
 
-@pytest.mark.parametrize("M,N,K", [(1000, 1000, 1000), (129, 257, 1040), (517, 95, 333)])
+@pytest.mark.parametrize("M,N,K", [(1000, 1000, 1000), (129, 257, 1040), (517, 95, 333), (300, 300, 100),
+                                   (600, 520, 2000)])
 def test_ragged_padded(cuda_device, M, N, K):
     run_case(M, N, K, "row", "col", pad=16)
     run_case(M, N, K, "col", "row", pad=32, out="f16")
@@ -92,8 +93,9 @@ def test_ragged_padded(cuda_device, M, N, K):
 
 @pytest.mark.parametrize("stream_k", [True, False])
 def test_stream_k_equivalence(cuda_device, stream_k):
-    # 148 SMs, 128x256 tiles: 19 x 20 = 380 tiles -> 2 full waves + stream-K tail
-    run_case(19 * 128, 20 * 256, 1024, stream_k=stream_k)
+    # 200 rows: fewer than a CTA-pair tile, too many to swap -> 1-CTA 128 x 256 tiles,
+    # 2 x 32 = 64 tiles over 148 SMs: all stream-K (or whole tiles without a workspace)
+    run_case(200, 8192, 1024, stream_k=stream_k)
 
 
 def test_stream_k_workspace_reuse(cuda_device):
