@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 namespace b2sq {
@@ -51,6 +52,9 @@ __device__ unsigned long long g_trace[4096 * 8];
 
 namespace {
 
+#ifndef B2SQ_PAIR_TMA_STORE
+#define B2SQ_PAIR_TMA_STORE 1  // pair-kernel output blocks leave by TMA bulk-tensor stores
+#endif
 #ifndef B2SQ_RASTER_GROUP
 #define B2SQ_RASTER_GROUP 16  // M tiles per raster group
 #endif
@@ -89,6 +93,7 @@ struct KParams {
     void* extra_c[kMaxExtraOut];  // further destinations of every store (all-gather)
     uint32_t n_extra;
     uint8_t* mc_c;  // multicast view of c (all-gather through NVSwitch), or null
+    uint32_t tma_store;  // 1: the pair kernel's staged output pieces leave by TMA bulk-tensor stores
     const float* row_scale_vec;
     const float* col_scale_vec;
     float row_scale, col_scale;
@@ -411,6 +416,22 @@ __device__ __forceinline__ uint4 lds128_epi(uint32_t addr)
 // NVLink moves peer stores (the all-gather build) at full rate only from
 // 128-byte runs (measured: 16-byte runs reach a quarter of it).  Same values
 // as store_chunk in every case.
+// TMA bulk-tensor store of one staged 32-row x 64-column (128-byte) block:
+// the staging layout (16-byte pieces XOR-swizzled by row) is the 128-byte
+// swizzle of a tensor map with box {64, 32}.  Issued by one lane after every
+// lane's shared-memory writes are ordered for the async proxy.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Output store of the staged path, marked evict-first (.cs): the output is
 // written once and not re-read by this kernel, so it should not push operand
 // tiles other CTAs still need out of L2 (measured 1-2% at 8192^2 x 2048).
@@ -422,12 +443,19 @@ __device__ __forceinline__ void st_out16(void* p, uint4 v)
 
 template <uint32_t W, bool G>
 __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint32_t col0, const int32_t (&a0)[W],
-                                           const int32_t (&a1)[W], float rsc, float cs0, float cs1, uint32_t stage)
+                                           const int32_t (&a1)[W], float rsc, float cs0, float cs1, uint32_t stage,
+                                           const CUtensorMap* tmC = nullptr, uint32_t block_row0 = 0,
+                                           bool block_whole = false)
 {
     if constexpr (W == 32) {
         if (stage != 0 && p.c_type != 2 && !p.transpose_out && p.vec_store_ok &&
             col0 + 2 * W <= p.Nk) {
             const uint32_t lane = threadIdx.x & 31;
+            const bool by_tma = !G && tmC != nullptr && block_whole;
+            if (!G && tmC != nullptr) {
+                if (lane == 0) bulk_wait_read0();  // the previous TMA store has read the staging area
+                __syncwarp();
+            }
             // row-major [32 rows][128 B], 16-byte pieces XOR-swizzled by row (conflict-free both
             // ways); pieces 0-3 from the first chunk, 4-7 from the second, each written as soon
             // as it is packed
@@ -447,6 +475,12 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
             };
             stage_chunk(a0, cs0, 0);
             stage_chunk(a1, cs1, 4);
+            if (by_tma) {
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) tma_store_2d(tmC, stage, (int32_t)col0, (int32_t)block_row0);
+                return;
+            }
             __syncwarp();
             const size_t ldc_bytes = (size_t)p.ldc * 2;
 #pragma unroll
@@ -836,8 +870,11 @@ constexpr uint32_t kPairHalfBytes = 128 * kPairBK;          // 16 KiB: one opera
 constexpr uint32_t kPairSB = 2 * kPairHalfBytes;            // A half + B half per CTA per stage
 constexpr uint32_t kPairST = 6;
 constexpr uint32_t kPairBarOff = kPairST * kPairSB;
-constexpr uint32_t kPairEpiOff = kPairBarOff + kBarrierBytes;
-constexpr uint32_t pair_smem(bool) { return kPairBarOff + kBarrierBytes + kEpiStageBytes + 1024; }
+// The staging area starts on a 1024-byte boundary: the TMA store's 128-byte
+// swizzle is a function of the shared-memory address bits.
+constexpr uint32_t kPairEpiOff = kPairBarOff + 1024;
+static_assert(kBarrierBytes <= 1024 && kPairEpiOff % 1024 == 0, "pair staging alignment");
+constexpr uint32_t pair_smem(bool) { return kPairEpiOff + kEpiStageBytes + 1024; }
 constexpr uint32_t kPairSmem = pair_smem(true);
 static_assert(kPairSmem <= kSmemBudget, "pair kernel shared memory overflow");
 
@@ -885,7 +922,7 @@ __device__ __forceinline__ PairTile pair_tile(const KParams& p, uint32_t t, cons
 template <bool kGrouped, bool G = false>
 __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const KParams p, uint64_t wait_limit_ns)
+                        const __grid_constant__ CUtensorMap tmC, const KParams p, uint64_t wait_limit_ns)
 {
     constexpr uint32_t ST = kPairST;
     constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
@@ -935,6 +972,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (!G && p.tma_store) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
         tmem_alloc_pair(smem_u32(const_cast<uint32_t*>(taddr_slot)), TMEM_COLS);
@@ -1020,6 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         const uint32_t row_local = q * 32 + lane;
         constexpr uint32_t CW = 32, NCH = kPairBN / CW;
         const uint32_t epi_stage = sbase + kPairEpiOff + q * 4096;
+        const CUtensorMap* tmc = (!G && p.tma_store) ? &tmC : nullptr;
         uint32_t uidx = 0;
         for (uint32_t t = pair; t < T; t += npairs, ++uidx) {
             const uint32_t buf = uidx & 1, use = uidx >> 1;
@@ -1049,9 +1088,15 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
                 }
-                store_pair<CW, G>(p, row, tg.col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage);
+                // TMA clips the matrix edges itself; a group's last block that
+                // ends inside the matrix is stored row by row instead
+                const uint32_t brow0 = tg.a_row + rank * 128 + q * 32;
+                store_pair<CW, G>(p, row, tg.col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage, tmc,
+                                  brow0, brow0 + 32 <= tg.row_end || tg.row_end >= p.Mk);
             }
         }
+        if (tmc != nullptr && lane == 0) bulk_wait_all();  // stores done before the CTA's shared memory goes
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -1146,9 +1191,29 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     return cudaGetLastError();
 }
 
-template <bool kGrouped, bool G = false>
-cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
+// Output map of the pair kernel's TMA stores: 16-bit elements, dims {Nk, Mk},
+// box {64 columns, 32 rows}, 128-byte swizzle (the staging layout).
+bool make_output_map(CUtensorMap* map, void* c, uint32_t Mk, uint32_t Nk, uint32_t ldc)
 {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {Nk, Mk};
+    cuuint64_t strides[1] = {(cuuint64_t)ldc * 2};
+    cuuint32_t box[2] = {64, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, c, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kGrouped, bool G = false>
+cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, cudaStream_t st)
+{
+    CUtensorMap tc;
+    std::memset(&tc, 0, sizeof(tc));
+    kp.tma_store = 0;
+    if (!G && B2SQ_PAIR_TMA_STORE && kp.c_type != 2 && !kp.transpose_out && kp.vec_store_ok)
+        kp.tma_store = make_output_map(&tc, kp.c, kp.Mk, kp.Nk, kp.ldc) ? 1u : 0u;
     static std::atomic<uint64_t> done_mask{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1160,7 +1225,7 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_pair_kernel<kGrouped, G><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_pair_kernel<kGrouped, G><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, tc, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
