@@ -8,18 +8,27 @@ One step = one b2sq_gemm_i8 call.  ``value`` is whole-job TOPS (2*M*N*K per
 step per rank) with inputs resident in HBM; L2 (126 MB) is flushed before
 every timed step, outside the timed events, by reading a 512 MB buffer (a
 read leaves no dirty lines whose write-back would land in the timed kernel).
-At N > 1 GPUs the GEMM is N-sharded (column-parallel weights, weak scaling:
-every rank owns an 8192-column weight shard and the same activations), the
-output stays N-sharded; there is no collective inside the timed step.
+At N > 1 GPUs the headline GEMM is N-sharded (column-parallel weights, weak
+scaling: every rank owns an 8192-column weight shard and the same
+activations), the output stays N-sharded; there is no collective inside its
+timed step.  The strong-scaling case is config 4, reported in ``c4`` (the last
+key of the line): the 16384 x 8192 x 28672 prefill GEMM timed on one GPU and
+N-sharded over all ranks, the whole step with smoothquant, and the output
+all-gather fused into the GEMM against NCCL, with a bit-exact comparison of
+the two gathered results (the run exits non-zero if they differ).
 
 Extra objects on the JSON line:
   roofline      the GEMM kernel against the int8 dense peak derived from the
-                measured bf16 peak (2x, MEASURED_PEAKS.json)
+                measured bf16 peak (2x, MEASURED_PEAKS.json), and against
+                torch._int_mm (cuBLASLt) at 8192^3 timed the same way
+  sustained     the same GEMM back to back for >= 2 s, with its SM clocks
   smoothquant   GB/s of b2sq_smoothquant at the prefill activation shape
                 16384 x 8192 (reference byte formula, rocwmma_smoothquant.cpp:157-158)
+  decode, moe_c5  configs 3 and 5 (N = 1 only; replicas at N > 1)
   e2e           the same GEMM through the C ABI from pinned host buffers:
                 H2D of A, B and scales + GEMM + D2H of C inside the timed region
   cpu_baseline  the CPU oracle (restated reference CPU path) on a row sample
+  c4            config 4, see above
 
 ``--impl reference`` times the reference's CPU path (the oracle restatement;
 the HIP reference cannot run on this machine) on the host cores, rank 0 only.
@@ -40,8 +49,8 @@ M = N = K = 8192
 FLUSH_BYTES = 512 << 20
 SQ_M, SQ_K = 16384, 8192
 
-# DRAM bytes (read + write) of one gemm_i8_pair_kernel launch at 8192^3, from
-# the ncu capture summarised in profiles/gemm_i8_pair_8192_ncu.md.
+# DRAM bytes (read + write) of one gemm_i8_pair_kernel launch at 8192^3,
+# from an ncu capture of `bench.py --profile gemm`.
 GEMM_TRAFFIC_BYTES = 341_518_592  # 225,995,776 read + 115,522,816 written
 
 
@@ -93,14 +102,15 @@ def measured_peaks():
 
 # ---------------------------------------------------------------- clocks (NVML)
 class ClockSampler:
-    """Samples SM clock and throttle reasons every 20 ms on a thread."""
+    """Samples SM clock and throttle reasons every `interval` s on a thread."""
 
     REASONS = {
         "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
         "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, local_rank: int):
+    def __init__(self, local_rank: int, interval: float = 0.001):
+        self.interval = interval
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
@@ -128,7 +138,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            time.sleep(0.02)
+            time.sleep(self.interval)
 
     def __enter__(self):
         if self._h is not None:
@@ -157,6 +167,8 @@ def cpu_gemm_sample(budget_s: float, seed: int = 0):
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
 
+    # every host core (torchrun sets OMP_NUM_THREADS=1 in each rank)
+    O.set_num_threads(len(os.sched_getaffinity(0)))
     rng = np.random.default_rng(seed)
     w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)  # [N, K] K-major
     sb = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
@@ -170,6 +182,20 @@ def cpu_gemm_sample(budget_s: float, seed: int = 0):
         if dt >= budget_s * 0.5 or rows >= M:
             return 2.0 * rows * N * K / dt / 1e12, rows, dt, O.num_threads()
         rows = min(M, max(rows * 2, int(rows * budget_s / max(dt, 1e-3))))
+
+
+def bench_config(world: int) -> dict:
+    """The workload named on both arms' lines."""
+    return {"workload": "c2_square_int8_gemm_8192", "M": M, "N": N, "K": K,
+            "a_layout": "row-major", "b_layout": "column-major (K-major weights)",
+            "scales": "per-row x per-column fp32", "out": "bf16",
+            "parallelism": f"n-sharded x{world}" if world > 1 else "single-gpu",
+            "l2": "flushed (512 MB read) before every timed step"}
+
+
+def r4(v):
+    """Four significant digits (keeps the JSON line short)."""
+    return None if v is None else float(f"{v:.4g}")
 
 
 # ---------------------------------------------------------------- reference arm
@@ -190,8 +216,7 @@ def run_reference(args, rank: int, world: int):
         "impl": "reference", "metric": "int8 GEMM TOPS at 8192^3 (M=N=K=8192, bf16 out)", "value": value,
         "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8->int32",
-        "data": "synthetic", "config": {"workload": "c2_square_int8_gemm_8192", "M": M, "N": N, "K": K,
-                                         "parallelism": "cpu-reference"},
+        "data": "synthetic", "config": bench_config(world),
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": thr, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference is HIP/rocWMMA (AMD only): its CPU path is restated in oracle/ and timed here",
@@ -227,6 +252,35 @@ def main():
 
     hbm_gbs, bf16_tflops, peak_src = measured_peaks()
     int8_peak = 2.0 * bf16_tflops
+    stream = torch.cuda.current_stream(dev)
+    flush_buf = torch.ones(FLUSH_BYTES // 8, dtype=torch.int64, device=dev)
+
+    def l2_flush():
+        flush_buf.sum()
+
+    def max_over_ranks(v: float) -> float:
+        t_ = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        return float(t_.item())
+
+    def timed(fn, n, flush=True):
+        """Mean device ms of fn over n steps (L2 flushed before each), max over ranks."""
+        for _ in range(3):
+            fn()
+        evs = []
+        barrier()
+        torch.cuda.synchronize()
+        for _ in range(n):
+            if flush:
+                l2_flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        return max_over_ranks(statistics.mean(a_.elapsed_time(b_) for a_, b_ in evs))
 
     # inputs: same activations on every rank, a distinct weight shard per rank
     a = synth.torch_int8_uniform((M, K), dev, 11)
@@ -235,12 +289,7 @@ def main():
     sa = synth.torch_scales(M, dev, 13)
     sb = synth.torch_scales(N, dev, 200 + rank)
     c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    flush_buf = torch.ones(FLUSH_BYTES // 8, dtype=torch.int64, device=dev)
-
-    def l2_flush():
-        flush_buf.sum()
     ws = api.Workspace()
-    stream = torch.cuda.current_stream(dev)
 
     def step():
         api.gemm_quant(a, b, sa, sb, out_dtype=torch.bfloat16, c=c, workspace=ws)
@@ -267,166 +316,44 @@ def main():
         raise RuntimeError("a bounded device wait timed out during the benchmark")
     step_ms = [e0.elapsed_time(e1) for e0, e1 in evs]
     ms = statistics.mean(step_ms)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(ms)
     ops = 2.0 * M * N * K
     value = world * ops / (ms_max * 1e-3) / 1e12
     achieved = ops / (ms * 1e-3) / 1e12
 
-    # ---------------- smoothquant at the prefill activation shape (HBM bound)
-    g = torch.Generator(device=dev)
-    g.manual_seed(3)
-    x = torch.randn((SQ_M, SQ_K), generator=g, device=dev).to(torch.float16)
-    s = torch.empty((SQ_K,), device=dev).uniform_(0.5, 2.0, generator=g)
-    y = torch.empty((SQ_M, SQ_K), dtype=torch.int8, device=dev)
-    rs = torch.empty((SQ_M,), dtype=torch.float32, device=dev)
-    for _ in range(5):
-        api.smoothquant(x, s, y=y, row_scale=rs)
-    sq_ms = []
-    for _ in range(50):
-        l2_flush()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        api.smoothquant(x, s, y=y, row_scale=rs)
-        e1.record(stream)
-        sq_ms.append((e0, e1))
-    torch.cuda.synchronize()
-    sq_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in sq_ms)
-    sq_bytes = SQ_M * SQ_K * 2 + SQ_M * SQ_K + SQ_K * 4 + SQ_M * 4
-    sq_gbs = sq_bytes / (sq_ms * 1e-3) / 1e9
-    del x, y
+    # ---------------- measured int8 ceiling: cuBLASLt (torch._int_mm) at 8192^3, timed the same way
+    def intmm():
+        torch._int_mm(a, b)
 
-    def timed(fn, n):
-        """Mean device ms of fn over n steps (L2 flushed before each), max over ranks."""
-        for _ in range(3):
-            fn()
-        evs = []
-        barrier()
-        for _ in range(n):
-            l2_flush()
+    ms_lt = timed(intmm, 10)
+    lt_tops = ops / (ms_lt * 1e-3) / 1e12
+
+    # ---------------- sustained: the same GEMM back to back for >= 2 s (no flush), clocks sampled
+    sus = None
+    if world == 1:
+        n_sus = max(50, int(2.0 / (ms_max * 1e-3)) + 1)
+        torch.cuda.synchronize()
+        with ClockSampler(local_rank, interval=0.01) as clk_sus:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            fn()
+            for _ in range(n_sus):
+                step()
             e1.record(stream)
-            evs.append((e0, e1))
-        torch.cuda.synchronize()
-        t_ = torch.tensor([statistics.mean(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
-        return float(t_.item())
+            torch.cuda.synchronize()
+        sus_ms = e0.elapsed_time(e1) / n_sus
+        cs = clk_sus.summary()
+        sus = {"tops": r4(ops / (sus_ms * 1e-3) / 1e12), "ms": r4(sus_ms), "steps": n_sus,
+               "seconds": r4(sus_ms * n_sus * 1e-3), "clocks": cs}
+        if cs:
+            # throughput per clock: compares burst and power-capped rates at equal frequency
+            sus["tops_per_ghz"] = r4(sus["tops"] / (cs["sm_mhz"] * 1e-3))
 
-    # ---------------- config 3: decode smoothquant + GEMM, HBM bound
-    decode = {}
-    w_dec = synth.torch_int8_uniform((28672, K), dev, 31)
-    sb_dec = synth.torch_scales(28672, dev, 32)
-    s_dec = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
-    for md in (16, 64):
-        x_dec = torch.randn((md, K), generator=g, device=dev).to(torch.float16)
-        y_dec = torch.empty((md, K), dtype=torch.int8, device=dev)
-        r_dec = torch.empty((md,), dtype=torch.float32, device=dev)
-        o_dec = torch.empty((md, 28672), dtype=torch.float16, device=dev)
+    extra = {}
+    if world == 1:
+        extra = n1_sections(args, dev, api, synth, timed, l2_flush, stream, hbm_gbs, ws)
 
-        def dec_step():  # one fused call: smoothquant, then the GEMM launched with PDL
-            api.smoothquant_gemm(x_dec, s_dec, w_dec, sb_dec, out_dtype=torch.float16, xq=y_dec, row_scale=r_dec,
-                                 c=o_dec, workspace=ws)
-
-        ms_d = timed(dec_step, 50)
-        bytes_d = (md * K * 2 + md * K + K * 4 + md * 4) + (md * K + 28672 * K + 4 * 28672 + 4 * md + 2 * md * 28672)
-        decode[f"m{md}"] = {"ms": ms_d, "gbs": world * bytes_d / (ms_d * 1e-3) / 1e9,
-                            "frac_of_measured_hbm": bytes_d / (ms_d * 1e-3) / 1e9 / hbm_gbs,
-                            "shape": [md, K, 28672], "gpu_launches_per_step": 2}
-    del w_dec
-
-    # ---------------- config 4: N-sharded prefill (smoothquant + GEMM), 16384 x 8192 x 28672
-    from optimized_rocwmma_samples_b200.sharded import ShardedPrefill, cuda_ops, shard_range
-
-    PM, PN = 16384, 28672
-    n0, n1 = shard_range(PN, world, rank)
-    w_pf = synth.torch_int8_uniform((n1 - n0, K), dev, 40 + rank)
-    sb_pf = synth.torch_scales(n1 - n0, dev, 50 + rank)
-    layer = ShardedPrefill(w_pf, sb_pf, PN, cuda_ops(torch.bfloat16))
-    x_pf = torch.randn((PM, K), generator=g, device=dev).to(torch.float16)
-    s_pf = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
-    ops_pf = 2.0 * PM * PN * K
-    ms_pf = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", False), 10)
-    xq_pf, rs_pf = api.smoothquant(x_pf, s_pf)
-    ms_gm = timed(lambda: layer.ops.gemm(xq_pf, layer.w, rs_pf, layer.sb), 10)
-    prefill = {"shape": [PM, K, PN], "shard_cols": n1 - n0,
-               "sharded_compute": {"ms": ms_pf, "tops": ops_pf / (ms_pf * 1e-3) / 1e12,
-                                   "note": "x replicated, each rank quantises and multiplies its N shard, "
-                                           "output left N-sharded"},
-               "sharded_gemm": {"ms": ms_gm, "tops": ops_pf / (ms_gm * 1e-3) / 1e12,
-                                "note": "the GEMM alone on each rank's N shard (max over ranks); "
-                                        "scaling = the 1-GPU ms / this"}}
-    del xq_pf, rs_pf
-    if world > 1:
-        ms_e = timed(lambda: layer.forward(x_pf if rank == 0 else None, s_pf, PM, K, "rank0", True), 5)
-        prefill["with_collectives"] = {"ms": ms_e, "tops": ops_pf / (ms_e * 1e-3) / 1e12,
-                                       "note": "rank 0 quantises, NCCL broadcast of Xq and row scales, "
-                                               "sharded GEMM, NCCL all-gather of the bf16 output into [M, N]"}
-        # GEMM -> all-gather of the output: NCCL after the GEMM vs fused into the GEMM's epilogue
-        ms_g = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", True), 5)
-        ms_f = timed(lambda: layer.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
-        from optimized_rocwmma_samples_b200.sharded import multicast_supported
-        mc = multicast_supported(dev)
-        ms_fm = None
-        if mc:
-            layer_mc = ShardedPrefill(w_pf, sb_pf, PN, cuda_ops(torch.bfloat16, gather="multicast"))
-            ms_fm = timed(lambda: layer_mc.forward(x_pf, s_pf, PM, K, "replicated", "fused"), 5)
-            layer_mc.ops.close()
-            del layer_mc
-        out_bytes = PM * PN * 2
-        prefill["gather_nccl"] = {"ms": ms_g, "tops": ops_pf / (ms_g * 1e-3) / 1e12,
-                                  "note": "x replicated, sharded GEMM, then NCCL all-gather into [M, N]"}
-        prefill["gather_fused"] = {"ms": ms_f, "tops": ops_pf / (ms_f * 1e-3) / 1e12,
-                                   "nvlink_bytes_out_per_gpu": out_bytes // world * (world - 1),
-                                   "nvlink_bytes_in_per_gpu": out_bytes // world * (world - 1),
-                                   "note": "x replicated, b2sq_gemm_i8_allgather: one GEMM whose epilogue stores "
-                                           "every output tile into each rank's [M, N] buffer over NVLink (CUDA IPC "
-                                           "mappings); one-element all-reduce barriers before and after"}
-        if ms_fm is not None:
-            prefill["gather_fused_multicast"] = {
-                "ms": ms_fm, "tops": ops_pf / (ms_fm * 1e-3) / 1e12,
-                "nvlink_bytes_out_per_gpu": out_bytes // world,
-                "note": "b2sq_gemm_i8_allgather_mc: each output piece stored once with multimem.st through "
-                        "the NVSwitch multicast mapping (torch symmetric memory); bound like the other by "
-                        "the bytes every GPU receives"}
-    layer.ops.close()
-    del layer, w_pf, x_pf
-
-    # ---------------- config 5: MoE, router -> sorting -> MoE smoothquant -> grouped GEMM (replicas)
-    T5, H5, E5, K5, N5 = synth.MOE_TOKENS, synth.MOE_HIDDEN, synth.MOE_EXPERTS, synth.MOE_TOPK, synth.MOE_INTER
-    logits5 = torch.randn((T5, E5), generator=g, device=dev).to(torch.float16)
-    x5 = torch.randn((T5, H5), generator=g, device=dev).to(torch.float16)
-    s5 = torch.empty((E5, H5), device=dev).uniform_(0.5, 2.0, generator=g)
-    w5 = synth.torch_int8_uniform((E5, N5, H5), dev, 55)
-    sb5 = synth.torch_scales(E5 * N5, dev, 56)
-    unit5 = 128  # expert segments padded to whole 128-row tiles
-    tw5, ti5 = api.topk_softmax(logits5, K5)
-    cnt5, st5, sid5, perm5 = api.moe_sorting(ti5, E5, unit5)
-    rows5 = T5 * K5 + E5 * unit5
-    qy5 = torch.zeros((rows5, H5), dtype=torch.int8, device=dev)
-    rs5 = torch.zeros((rows5,), dtype=torch.float32, device=dev)
-    out5 = torch.empty((rows5, N5), dtype=torch.bfloat16, device=dev)
-
-    def moe_step():
-        api.topk_softmax(logits5, K5, tw5, ti5)
-        cnt, st, _, perm = api.moe_sorting(ti5, E5, unit5)
-        api.moe_smoothquant(x5, s5, ti5, qy=qy5, row_scale=rs5, row_perm=perm, out_rows=rows5)
-        api.gemm_grouped(qy5, w5, st, cnt, rs5, sb5, out_dtype=torch.bfloat16, c=out5)
-
-    ms_moe = timed(moe_step, 10)
-    ms_grp = timed(lambda: api.gemm_grouped(qy5, w5, st5, cnt5, rs5, sb5, out_dtype=torch.bfloat16, c=out5), 10)
-    ops5 = 2.0 * T5 * K5 * N5 * H5
-    moe = {"shape": {"tokens": T5, "hidden": H5, "experts": E5, "topk": K5, "inter": N5},
-           "pipeline_ms": ms_moe, "grouped_gemm_ms": ms_grp,
-           "grouped_gemm_tops": ops5 / (ms_grp * 1e-3) / 1e12, "pipeline_tops": ops5 / (ms_moe * 1e-3) / 1e12,
-           "gpu_launches_per_step": 4,
-           "note": "router (b2sq_topk_softmax) -> b2sq_moe_sorting -> MoE smoothquant into expert order -> "
-                   "b2sq_gemm_i8_grouped, all on the device; replicas at N > 1"}
-    del w5, qy5, out5
+    # ---------------- config 4: N-sharded prefill (strong scaling over the ranks)
+    c4 = c4_section(dev, world, rank, api, synth, timed)
 
     # ---------------- e2e through the C ABI from pinned host buffers
     h_a = a.cpu().pin_memory()
@@ -452,11 +379,8 @@ def main():
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * ops / (float(t.item()) * 1e-3) / 1e12
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_value = world * ops / (e2e_ms * 1e-3) / 1e12
     h2d = a.numel() + w.numel() + 4 * (sa.numel() + sb.numel())
     d2h = c.numel() * 2
 
@@ -473,29 +397,171 @@ def main():
             "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8->int32", "data": "synthetic",
-            "config": {"workload": "c2_square_int8_gemm_8192", "M": M, "N": N, "K": K,
-                       "a_layout": "row-major", "b_layout": "column-major (K-major weights)",
-                       "scales": "per-row x per-column fp32", "out": "bf16",
-                       "parallelism": f"n-sharded x{world}" if world > 1 else "single-gpu",
-                       "l2": "flushed (512 MB read) before every timed step"},
+            "config": bench_config(world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
                          "frac": achieved / int8_peak, "traffic": GEMM_TRAFFIC_BYTES,
-                         "peak_note": f"2 x {peak_src} bf16 dense {bf16_tflops} TFLOP/s (int8 dense rate = 2x bf16); "
-                                      f"nominal int8 4500 TOPS -> frac {achieved / 4500.0:.3f}"},
-            "smoothquant": {"shape": [SQ_M, SQ_K], "ms": sq_ms, "gbs": sq_gbs,
-                            "frac_of_measured_hbm": sq_gbs / hbm_gbs, "hbm_peak_gbs": hbm_gbs},
-            "decode": decode,
-            "prefill_c4": prefill,
-            "moe_c5": moe,
+                         "peak_int8_measured": r4(lt_tops), "frac_vs_measured_int8": r4(achieved / lt_tops),
+                         "frac_vs_nominal_int8": r4(achieved / 4500.0),
+                         "peak_note": f"peak = 2 x {peak_src} bf16 dense {bf16_tflops} TFLOP/s; "
+                                      "peak_int8_measured = torch._int_mm (cuBLASLt) 8192^3, int32 out, "
+                                      "L2 flushed, same box"},
             "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
-            "wall_s_timed": t_wall,
+            "wall_s_timed": r4(t_wall),
             "cpu_baseline": cpu,
         }
+        if sus is not None:
+            line["sustained"] = sus
+        line.update(extra)
+        line["c4"] = c4  # last: the driver keeps the tail of the line
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    if c4.get("gather_parity") is False:
+        sys.exit(3)
+
+
+def n1_sections(args, dev, api, synth, timed, l2_flush, stream, hbm_gbs, ws):
+    """Smoothquant, decode (config 3) and MoE (config 5) on one GPU."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    out = {}
+    # ---------------- smoothquant at the prefill activation shape (HBM bound)
+    x = torch.randn((SQ_M, SQ_K), generator=g, device=dev).to(torch.float16)
+    s = torch.empty((SQ_K,), device=dev).uniform_(0.5, 2.0, generator=g)
+    y = torch.empty((SQ_M, SQ_K), dtype=torch.int8, device=dev)
+    rs = torch.empty((SQ_M,), dtype=torch.float32, device=dev)
+    sq_ms = timed(lambda: api.smoothquant(x, s, y=y, row_scale=rs), 50)
+    sq_bytes = SQ_M * SQ_K * 2 + SQ_M * SQ_K + SQ_K * 4 + SQ_M * 4
+    sq_gbs = sq_bytes / (sq_ms * 1e-3) / 1e9
+    out["smoothquant"] = {"shape": [SQ_M, SQ_K], "ms": r4(sq_ms), "gbs": r4(sq_gbs),
+                          "frac_of_measured_hbm": r4(sq_gbs / hbm_gbs), "hbm_peak_gbs": hbm_gbs}
+    del x, y
+
+    # ---------------- config 3: decode smoothquant + GEMM, HBM bound
+    decode = {}
+    w_dec = synth.torch_int8_uniform((28672, K), dev, 31)
+    sb_dec = synth.torch_scales(28672, dev, 32)
+    s_dec = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
+    for md in (16, 64):
+        x_dec = torch.randn((md, K), generator=g, device=dev).to(torch.float16)
+        y_dec = torch.empty((md, K), dtype=torch.int8, device=dev)
+        r_dec = torch.empty((md,), dtype=torch.float32, device=dev)
+        o_dec = torch.empty((md, 28672), dtype=torch.float16, device=dev)
+
+        def dec_step():  # one fused call: smoothquant and the GEMM
+            api.smoothquant_gemm(x_dec, s_dec, w_dec, sb_dec, out_dtype=torch.float16, xq=y_dec, row_scale=r_dec,
+                                 c=o_dec, workspace=ws)
+
+        ms_d = timed(dec_step, 50)
+        bytes_d = (md * K * 2 + md * K + K * 4 + md * 4) + (md * K + 28672 * K + 4 * 28672 + 4 * md + 2 * md * 28672)
+        decode[f"m{md}"] = {"ms": r4(ms_d), "gbs": r4(bytes_d / (ms_d * 1e-3) / 1e9),
+                            "frac_of_measured_hbm": r4(bytes_d / (ms_d * 1e-3) / 1e9 / hbm_gbs),
+                            "shape": [md, K, 28672], "gpu_launches_per_step": 2}
+    out["decode"] = decode
+    del w_dec
+
+    # ---------------- config 5: MoE, router -> sorting -> MoE smoothquant -> grouped GEMM
+    T5, H5, E5, K5, N5 = synth.MOE_TOKENS, synth.MOE_HIDDEN, synth.MOE_EXPERTS, synth.MOE_TOPK, synth.MOE_INTER
+    logits5 = torch.randn((T5, E5), generator=g, device=dev).to(torch.float16)
+    x5 = torch.randn((T5, H5), generator=g, device=dev).to(torch.float16)
+    s5 = torch.empty((E5, H5), device=dev).uniform_(0.5, 2.0, generator=g)
+    w5 = synth.torch_int8_uniform((E5, N5, H5), dev, 55)
+    sb5 = synth.torch_scales(E5 * N5, dev, 56)
+    unit5 = 128  # expert segments padded to whole 128-row tiles
+    tw5, ti5 = api.topk_softmax(logits5, K5)
+    cnt5, st5, sid5, perm5 = api.moe_sorting(ti5, E5, unit5)
+    rows5 = T5 * K5 + E5 * unit5
+    qy5 = torch.zeros((rows5, H5), dtype=torch.int8, device=dev)
+    rs5 = torch.zeros((rows5,), dtype=torch.float32, device=dev)
+    out5 = torch.empty((rows5, N5), dtype=torch.bfloat16, device=dev)
+
+    def moe_step():
+        api.topk_softmax(logits5, K5, tw5, ti5)
+        cnt, st, _, perm = api.moe_sorting(ti5, E5, unit5)
+        api.moe_smoothquant(x5, s5, ti5, qy=qy5, row_scale=rs5, row_perm=perm, out_rows=rows5)
+        api.gemm_grouped(qy5, w5, st, cnt, rs5, sb5, out_dtype=torch.bfloat16, c=out5)
+
+    ms_moe = timed(moe_step, 10)
+    ms_grp = timed(lambda: api.gemm_grouped(qy5, w5, st5, cnt5, rs5, sb5, out_dtype=torch.bfloat16, c=out5), 10)
+    ops5 = 2.0 * T5 * K5 * N5 * H5
+    out["moe_c5"] = {"shape": {"tokens": T5, "hidden": H5, "experts": E5, "topk": K5, "inter": N5},
+                     "pipeline_ms": r4(ms_moe), "grouped_gemm_ms": r4(ms_grp),
+                     "grouped_gemm_tops": r4(ops5 / (ms_grp * 1e-3) / 1e12),
+                     "pipeline_tops": r4(ops5 / (ms_moe * 1e-3) / 1e12), "gpu_launches_per_step": 4}
+    return out
+
+
+# Peer copy bandwidth per direction measured on this pool's B200s (GB/s): the
+# ingress bound of an all-gather is (world-1)/world of the output at this rate.
+PEER_GBS = 770.0
+
+
+def c4_section(dev, world, rank, api, synth, timed):
+    """Config 4: 16384 x 8192 x 28672, smoothquant + int8 GEMM, N-sharded.
+
+    t1_*: the whole N on one GPU (every rank runs it alone, max over ranks);
+    tN_*: this rank's N shard with every rank at once.  *_gemm: the GEMM
+    alone; *_step: x -> smoothquant -> GEMM, output left N-sharded.  At N > 1
+    also the output all-gather: fused into the GEMM's epilogue
+    (b2sq_gemm_i8_allgather) and GEMM + NCCL all_gather_into_tensor (shards
+    left blocked, no re-layout copy), compared bit for bit."""
+    import torch
+    from optimized_rocwmma_samples_b200.sharded import ShardedPrefill, cuda_ops, shard_range
+
+    PM, PN = 16384, 28672
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    x = torch.randn((PM, K), generator=g, device=dev).to(torch.float16)
+    s = torch.empty((K,), device=dev).uniform_(0.5, 2.0, generator=g)
+    ops_pf = 2.0 * PM * PN * K
+    out = {"shape": [PM, K, PN], "n_gpus": world}
+    xq, rs = api.smoothquant(x, s)
+    # one GPU, whole N
+    w_full = synth.torch_int8_uniform((PN, K), dev, 40)
+    sb_full = synth.torch_scales(PN, dev, 50)
+    c_full = torch.empty((PM, PN), dtype=torch.bfloat16, device=dev)
+    t1_gemm = timed(lambda: api.gemm_quant(xq, w_full.t(), rs, sb_full, out_dtype=torch.bfloat16, c=c_full), 5)
+    xq1, rs1 = torch.empty_like(xq), torch.empty_like(rs)
+
+    def step1():
+        api.smoothquant(x, s, y=xq1, row_scale=rs1)
+        api.gemm_quant(xq1, w_full.t(), rs1, sb_full, out_dtype=torch.bfloat16, c=c_full)
+
+    t1_step = timed(step1, 5)
+    n0, n1 = shard_range(PN, world, rank)
+    w_sh = w_full[n0:n1].contiguous()
+    sb_sh = sb_full[n0:n1].contiguous()
+    del w_full, c_full, xq1, rs1
+    layer = ShardedPrefill(w_sh, sb_sh, PN, cuda_ops(torch.bfloat16))
+    tN_gemm = timed(lambda: layer.ops.gemm(xq, layer.w, rs, layer.sb), 10)
+    tN_step = timed(lambda: layer.forward(x, s, PM, K, "replicated", False), 10)
+    out.update({"t1_gemm_ms": r4(t1_gemm), "tN_gemm_ms": r4(tN_gemm), "speedup_sharded_gemm": r4(t1_gemm / tN_gemm),
+                "t1_step_ms": r4(t1_step), "tN_step_ms": r4(tN_step), "speedup_step": r4(t1_step / tN_step),
+                "tN_gemm_tops": r4(ops_pf / (tN_gemm * 1e-3) / 1e12)})
+    if world > 1:
+        t_fused = timed(lambda: layer.forward(x, s, PM, K, "replicated", "fused"), 5)
+        t_nccl = timed(lambda: layer.forward(x, s, PM, K, "replicated", "blocked"), 5)
+        # parity: the fused all-gather against NCCL's, bit for bit, on every rank
+        fused = layer.forward(x, s, PM, K, "replicated", "fused")
+        blocked = layer.forward(x, s, PM, K, "replicated", "blocked")
+        torch.cuda.synchronize()
+        wsh = PN // world
+        same = bool(torch.equal(fused.view(PM, world, wsh).view(torch.int16),
+                                blocked.permute(1, 0, 2).view(torch.int16)))
+        flag = torch.tensor([0 if same else 1], dtype=torch.int32, device=dev)
+        torch.distributed.all_reduce(flag)
+        out_bytes = PM * PN * 2
+        out.update({"gather_fused_ms": r4(t_fused), "gather_nccl_ms": r4(t_nccl),
+                    "ingress_bound_ms": r4(out_bytes * (world - 1) / world / (PEER_GBS * 1e9) * 1e3),
+                    "gather_parity": int(flag.item()) == 0})
+        del fused, blocked
+    layer.ops.close()
+    return out
+
 
 
 if __name__ == "__main__":

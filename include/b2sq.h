@@ -142,13 +142,15 @@ B2SQ_API b2sq_status b2sq_gemm_i8(uint32_t m, uint32_t n, uint32_t k,
  * the request path.  The stream-K scratch comes from a fixed 24 MiB array
  * compiled into the library, resident on every GPU that loads it until the
  * process exits; nothing is allocated.  Shapes whose schedule needs more
- * scratch than that return B2SQ_ERR_UNSUPPORTED (use b2sq_gemm_i8 with a
- * workspace); every shape whose tiles are at most 128 wide fits, and so
+ * scratch than that return B2SQ_ERR_UNSUPPORTED (b2sq_gemm_i8 with a null
+ * workspace runs them whole-tile, allocating nothing either); every shape whose tiles are at most 128 wide fits, and so
  * does every shape whose schedule needs no stream-K.  Arguments and results are those of b2sq_gemm_i8.
  * The first call on a device looks up the array's device address (once per
  * device); make that first call before any stream capture.  Every call
  * shares the array and clears its counters itself: calls that overlap on the
- * GPU (other streams or unordered host threads) race on it.
+ * GPU (other streams or unordered host threads) race on it.  The cached
+ * address belongs to the device's current context: after cudaDeviceReset
+ * this entry point must not be called again in the same process.
  */
 B2SQ_API b2sq_status b2sq_gemm_i8_no_alloc(uint32_t m, uint32_t n, uint32_t k,
                                            const int8_t* a, b2sq_layout la, uint32_t lda,

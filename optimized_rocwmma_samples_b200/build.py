@@ -78,7 +78,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         objs = list(ex.map(lambda s: _compile(s, verbose), _sources()))
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
-           "-Xlinker", "--no-undefined", "-lcuda" if False else "-ldl"]
+           "-Xlinker", "--no-undefined", "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

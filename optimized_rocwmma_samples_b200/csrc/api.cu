@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 namespace {
 
@@ -127,6 +128,44 @@ b2sq_status validate_gemm(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b
 }  // namespace
 
 b2sq_status b2sq::set_last_error(b2sq_status s, const char* msg) { return fail(s, "%s", msg); }
+
+namespace {
+std::mutex& status_mu()
+{
+    static std::mutex mu;
+    return mu;
+}
+std::vector<b2sq::StatusReader>& status_readers()
+{
+    static std::vector<b2sq::StatusReader> v;  // constructed on first use, before any registration
+    return v;
+}
+}  // namespace
+
+void b2sq::register_status_reader(StatusReader reader)
+{
+    std::lock_guard<std::mutex> lock(status_mu());
+    status_readers().push_back(reader);
+}
+
+// Reads and clears every translation unit's status word; *first_site gets the
+// first non-zero site code found (0 if none).
+cudaError_t b2sq::read_and_clear_all_status(cudaStream_t st, uint32_t* first_site)
+{
+    std::vector<StatusReader> rs;
+    {
+        std::lock_guard<std::mutex> lock(status_mu());
+        rs = status_readers();
+    }
+    *first_site = 0;
+    for (StatusReader r : rs) {
+        uint32_t v = 0;
+        cudaError_t e = r(st, &v);
+        if (e != cudaSuccess) return e;
+        if (*first_site == 0) *first_site = v;
+    }
+    return cudaSuccess;
+}
 
 extern "C" {
 
@@ -522,10 +561,7 @@ b2sq_status b2sq_gemm_i8_grouped(uint32_t groups, uint32_t rows, uint32_t n, uin
 b2sq_status b2sq_last_device_error(b2sq_stream_t stream, uint32_t* where)
 {
     uint32_t v = 0;
-    uint32_t v_sq = 0;
-    cudaError_t e = b2sq::read_and_clear_device_status(reinterpret_cast<cudaStream_t>(stream), &v);
-    if (e == cudaSuccess) e = b2sq::read_and_clear_sq_status(reinterpret_cast<cudaStream_t>(stream), &v_sq);
-    if (e == cudaSuccess && v == 0) v = v_sq;
+    cudaError_t e = b2sq::read_and_clear_all_status(reinterpret_cast<cudaStream_t>(stream), &v);
     if (e != cudaSuccess) return cuda_fail(e, "last_device_error");
     if (where) *where = v;
     if (v != 0) return fail(B2SQ_ERR_TIMEOUT, "device wait gave up at site %u", v);

@@ -9,6 +9,8 @@
 
 #include <utility>
 
+#include "kernels.h"
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "libb2sq is built for sm_100a only"
 #endif
@@ -20,8 +22,10 @@ namespace b2sq {
 // (first writer wins) and the kernel unwinds; the host reads it back with
 // b2sq_last_device_error().  Nothing traps.
 // ---------------------------------------------------------------------------
-// Whole-program compilation gives every translation unit its own copy; all
-// bounded waits and the host-side reader live in gemm_i8.cu.
+// Whole-program compilation gives every translation unit that includes this
+// header its own copy.  Each copy registers a host-side reader for itself at
+// load time (below), and b2sq_last_device_error() reads and clears every
+// registered copy, so a kernel in any translation unit is reported.
 static __device__ uint32_t g_device_status = 0;
 
 enum WaitSite : uint32_t {
@@ -51,6 +55,27 @@ __device__ __forceinline__ void record_timeout(uint32_t site)
 {
     atomicCAS(&g_device_status, 0u, site);
 }
+
+namespace {
+// Reads this translation unit's status word and clears it if it was set.
+cudaError_t read_and_clear_tu_status(cudaStream_t st, uint32_t* value)
+{
+    uint32_t v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && v != 0) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    *value = v;
+    return e;
+}
+struct StatusRegistrar {
+    StatusRegistrar() { register_status_reader(&read_and_clear_tu_status); }
+};
+StatusRegistrar g_status_registrar;
+}  // namespace
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
 {

@@ -42,14 +42,6 @@
 
 namespace b2sq {
 
-// Optional per-CTA timeline for experiments (compiled only with -DB2SQ_TRACE).
-#ifdef B2SQ_TRACE
-__device__ unsigned long long g_trace[4096 * 8];
-#define B2SQ_TRACE_POINT(i) (g_trace[blockIdx.x * 8 + (i)] = globaltimer_ns())
-#else
-#define B2SQ_TRACE_POINT(i) ((void)0)
-#endif
-
 namespace {
 
 #ifndef B2SQ_PAIR_TMA_STORE
@@ -539,7 +531,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        B2SQ_TRACE_POINT(0);
         for (uint32_t s = 0; s < ST; ++s) {
             mbar_init(full_bar + 8 * s, 1);
             mbar_init(empty_bar + 8 * s, 1);
@@ -578,7 +569,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tiles_total = s_gpre[p.groups];
     }
     const uint32_t tmem_base = *taddr_slot;
-    if (threadIdx.x == 0) B2SQ_TRACE_POINT(1);
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -779,7 +769,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
-                if (ethread == 0) B2SQ_TRACE_POINT(2);
                 // Stream-K partial: store it to this CTA's slot ([BN][128],
                 // column-major so a warp's stores are 128-byte coalesced).
                 int32_t* my_slot = p.ws_slots + ((size_t)blockIdx.x * 2 + u.slot) * TILE_ELEMS;
@@ -838,13 +827,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
-    if (threadIdx.x == 64) B2SQ_TRACE_POINT(3);
-    if (threadIdx.x == 32) B2SQ_TRACE_POINT(4);
     tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0) B2SQ_TRACE_POINT(5);
-    if (threadIdx.x == 64) B2SQ_TRACE_POINT(6);
-    if (threadIdx.x == 32) B2SQ_TRACE_POINT(7);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
@@ -1437,22 +1421,6 @@ cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st)
 {
     debug_wait_kernel<<<1, 32, 0, st>>>(limit_ns);
     return cudaGetLastError();
-}
-
-cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value)
-{
-    uint32_t v = 0;
-    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) return e;
-    e = cudaStreamSynchronize(st);
-    if (e != cudaSuccess) return e;
-    if (v != 0) {
-        const uint32_t zero = 0;
-        e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    }
-    *value = v;
-    return e;
 }
 
 }  // namespace b2sq

@@ -29,7 +29,9 @@ static __device__ __align__(256) unsigned char g_gemm_scratch[kStaticScratchByte
 
 // Device address of g_gemm_scratch on the current device.  In host code the
 // name g_gemm_scratch is only a host-side stand-in, so the address is looked
-// up once per device, with that device current.
+// up once per device, with that device current.  The cache assumes the
+// device's context lives as long as the process: after cudaDeviceReset the
+// address is stale and the entry point must not be called again.
 cudaError_t scratch_address(void** out)
 {
     static std::mutex mu;
@@ -68,7 +70,7 @@ B2SQ_API b2sq_status b2sq_gemm_i8_no_alloc(uint32_t m, uint32_t n, uint32_t k, c
             char msg[224];
             std::snprintf(msg, sizeof(msg),
                           "gemm_i8_no_alloc: this shape needs %zu bytes of scratch, more than the library's "
-                          "fixed %zu; use b2sq_gemm_i8 with a caller-provided workspace",
+                          "fixed %zu; b2sq_gemm_i8 with a null workspace runs it without scratch (whole tiles)",
                           need, kStaticScratchBytes);
             return b2sq::set_last_error(B2SQ_ERR_UNSUPPORTED, msg);
         }

@@ -116,9 +116,12 @@ cudaError_t launch_topk_softmax(const void* logits, float* topk_w, int32_t* topk
 // Debug: a kernel that waits for an mbarrier nobody arrives on, with a limit.
 cudaError_t launch_debug_bounded_wait(uint64_t limit_ns, cudaStream_t st);
 
-// Device status word access.
-cudaError_t read_and_clear_device_status(cudaStream_t st, uint32_t* value);  // gemm_i8.cu
-cudaError_t read_and_clear_sq_status(cudaStream_t st, uint32_t* value);      // smoothquant.cu
+// Device status words: every translation unit that includes common.cuh has
+// its own copy and registers a reader for it at load time (common.cuh);
+// b2sq_last_device_error() calls every registered reader (api.cu).
+using StatusReader = cudaError_t (*)(cudaStream_t st, uint32_t* value);
+void register_status_reader(StatusReader reader);
+cudaError_t read_and_clear_all_status(cudaStream_t st, uint32_t* first_site);
 
 // Sets the calling thread's message returned by b2sq_last_error_message()
 // and returns s (defined in api.cu).

@@ -786,20 +786,6 @@ bool use_tma(uint64_t rows, uint32_t row_elems, uint32_t& vpt)
 
 }  // namespace
 
-cudaError_t read_and_clear_sq_status(cudaStream_t st, uint32_t* value)
-{
-    uint32_t v = 0;
-    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_device_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    if (e == cudaSuccess && v != 0) {
-        const uint32_t zero = 0;
-        e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    }
-    *value = v;
-    return e;
-}
-
 cudaError_t launch_smoothquant(const void* x, const float* s, int8_t* y, float* rs, uint32_t M, uint32_t N, float qmax,
                                cudaStream_t st, int* used_vector_path)
 {

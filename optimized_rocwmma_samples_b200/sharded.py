@@ -198,16 +198,20 @@ class ShardedPrefill:
         dist.broadcast(rs, 0, group=self.group)
         return xq, rs
 
-    def gather(self, out_shard: torch.Tensor) -> torch.Tensor:
-        """All-gather the N shards into a row-major [M, N] tensor."""
+    def gather(self, out_shard: torch.Tensor, blocked: bool = False) -> torch.Tensor:
+        """All-gather the N shards.  blocked=False: a row-major [M, N] tensor;
+        blocked=True (equal shard widths only): the shards as they arrive,
+        [world, M, width], with no re-layout copy after the collective."""
         if self.world == 1:
-            return out_shard
+            return out_shard.unsqueeze(0) if blocked else out_shard
         m = out_shard.shape[0]
         widths = [b - a for a, b in self.shards]
+        if blocked and len(set(widths)) != 1:
+            raise ValueError("a blocked gather needs equal shard widths")
         if len(set(widths)) == 1 and dist.get_backend(self.group) == "nccl":
             buf = torch.empty((self.world, m, widths[0]), dtype=out_shard.dtype, device=out_shard.device)
             dist.all_gather_into_tensor(buf, out_shard.contiguous(), group=self.group)
-            return buf.permute(1, 0, 2).reshape(m, self.n_total)
+            return buf if blocked else buf.permute(1, 0, 2).reshape(m, self.n_total)
         # Unequal shards (or a backend without all_gather_into_tensor): pad
         # every shard to the widest, gather byte views, crop.
         wmax = max(widths)
@@ -215,17 +219,22 @@ class ShardedPrefill:
         mine[:, :out_shard.shape[1]] = out_shard
         parts = [torch.empty((m, wmax), dtype=out_shard.dtype, device=out_shard.device) for _ in widths]
         dist.all_gather([p.view(torch.uint8) for p in parts], mine.view(torch.uint8), group=self.group)
+        if blocked:
+            return torch.stack(parts)
         return torch.cat([p[:, :w_] for p, w_ in zip(parts, widths)], dim=1)
 
     def forward(self, x: Optional[torch.Tensor], smooth: torch.Tensor, m: int, k: int,
                 x_source: str = "replicated", gather_output=False) -> torch.Tensor:
-        """gather_output: False (N-sharded result), True (GEMM then all-gather)
-        or "fused" (the GEMM's epilogue gathers; the returned buffer is reused
-        by the next fused call of the same shape)."""
+        """gather_output: False (N-sharded result), True (GEMM then all-gather
+        into [M, N]), "blocked" (GEMM then all-gather, shards left as
+        [world, M, width]) or "fused" (the GEMM's epilogue gathers; the
+        returned buffer is reused by the next fused call of the same shape)."""
         xq, rs = self.quantize(x, smooth, x_source, m, k)
         if gather_output == "fused" and self.world > 1:
             if self.ops.gemm_gather is None:
                 raise ValueError("these ops have no fused GEMM + all-gather step")
             return self.ops.gemm_gather(xq, self.w, rs, self.sb, self.shards[self.rank][0], self.n_total, self)
         out = self.ops.gemm(xq, self.w, rs, self.sb)
+        if gather_output == "blocked":
+            return self.gather(out, blocked=True)
         return self.gather(out) if gather_output else out

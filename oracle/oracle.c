@@ -304,6 +304,18 @@ void oracle_topk_softmax(const uint16_t* logits, float* topk_w, int32_t* topk_i,
     }
 }
 
+/* Thread count of the parallel loops started from the calling thread
+ * (torchrun sets OMP_NUM_THREADS=1 in every rank; the timed CPU baseline
+ * sets it back to the host's core count). */
+void oracle_set_num_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int oracle_num_threads(void)
 {
 #ifdef _OPENMP

@@ -47,6 +47,7 @@ def load() -> C.CDLL:
         lib.oracle_float_to_bf16.argtypes = [f32]
         lib.oracle_float_to_bf16.restype = C.c_uint16
         lib.oracle_num_threads.restype = i
+        lib.oracle_set_num_threads.argtypes = [i]
         lib.oracle_topk_softmax.argtypes = [vp, vp, vp, u32, u32, u32]
         lib.oracle_route_exp.argtypes = [f32]
         lib.oracle_route_exp.restype = f32
@@ -60,6 +61,11 @@ def _p(a):
 
 def num_threads() -> int:
     return load().oracle_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    """Thread count of the oracle's parallel loops started from this thread."""
+    load().oracle_set_num_threads(int(n))
 
 
 def smoothquant(x: np.ndarray, smooth: np.ndarray, qmax: float = 127.0):

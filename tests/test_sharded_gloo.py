@@ -66,6 +66,11 @@ def worker(rank, world, port, q):
         out["rank0_gather"] = layer.forward(xin, torch.from_numpy(s), M, K, "rank0", True)
         out["rank0_shard"] = layer.forward(xin, torch.from_numpy(s), M, K, "rank0", False)
         out["repl_fused"] = layer.forward(torch.from_numpy(x), torch.from_numpy(s), M, K, "replicated", "fused")
+        # equal shards (the first 1024 columns): the blocked gather keeps [world, M, width]
+        e0, e1 = shard_range(1024, world, rank)
+        layer_eq = ShardedPrefill(torch.from_numpy(w[e0:e1].copy()), torch.from_numpy(sb[e0:e1].copy()), 1024,
+                                  oracle_ops())
+        out["repl_blocked"] = layer_eq.forward(torch.from_numpy(x), torch.from_numpy(s), M, K, "replicated", "blocked")
         q.put((rank, {k: v.numpy() for k, v in out.items()}, (n0, n1)))
     finally:
         dist.destroy_process_group()
@@ -109,3 +114,6 @@ def test_two_rank_sharded_prefill_matches_single_process():
         assert np.array_equal(out["rank0_gather"], full)
         assert np.array_equal(out["rank0_shard"], full[:, n0:n1])
         assert np.array_equal(out["repl_fused"], full)
+        blk = out["repl_blocked"]
+        assert blk.shape == (world, M, 1024 // world)
+        assert np.array_equal(blk.transpose(1, 0, 2).reshape(M, 1024), full[:, :1024])
