@@ -180,6 +180,35 @@ B2SQ_API b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* sm
                                               void* workspace, size_t workspace_bytes,
                                               b2sq_stream_t stream);
 
+/*
+ * The quantized GEMM for operands and result in HOST memory (replaces the
+ * reference driver's copy-in / kernel / copy-back sequence,
+ * rocwmma_gemm_quantized.cpp:214-218):
+ *   h_c[m, n] = cvt(float(h_a @ h_w^T) * (sa_i * sb_j))
+ * with h_a int8 [m, k] row-major, h_w int8 [n, k] (K-major weights = B
+ * column-major), scales as in b2sq_gemm_i8 (vectors may be null), h_c
+ * row-major.  The problem is cut into row_chunks x col_chunks output blocks
+ * (0 = chosen from the shape); the host->device copies, the block GEMMs and
+ * the device->host copies of finished blocks overlap on the caller's stream
+ * and two copy streams the library keeps per device.  dev_buffer (256-byte
+ * aligned, b2sq_gemm_i8_host_buffer_size bytes) holds the device copies;
+ * nothing is allocated.  Host memory should be pinned for the copies to
+ * overlap.  Enqueues only: h_c is complete once `stream` has been
+ * synchronised.  k % 16 == 0.  One call at a time per device.
+ */
+B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k,
+                                       const int8_t* h_a, const int8_t* h_w,
+                                       const float* h_scale_a_row, const float* h_scale_b_col,
+                                       float scale_a, float scale_b,
+                                       void* h_c, b2sq_dtype c_type,
+                                       void* dev_buffer, size_t dev_buffer_bytes,
+                                       uint32_t row_chunks, uint32_t col_chunks,
+                                       b2sq_stream_t stream);
+
+/* Device buffer bytes b2sq_gemm_i8_host needs for a shape. */
+B2SQ_API b2sq_status b2sq_gemm_i8_host_buffer_size(uint32_t m, uint32_t n, uint32_t k, b2sq_dtype c_type,
+                                                   size_t* bytes);
+
 /* Bytes of workspace that let b2sq_gemm_i8 use stream-K for this shape
  * (0 when the chosen schedule never splits a tile).  Host only. */
 B2SQ_API b2sq_status b2sq_gemm_i8_workspace_size(uint32_t m, uint32_t n, uint32_t k,

@@ -63,6 +63,9 @@ SIGNATURES = {
                                    _vp, _vp, _f32, _f32, _vp]),
     "b2sq_smoothquant_gemm_i8": (_i, [_vp, _vp, _f32, _vp, _vp, _u32, _u32, _vp, _i, _u32, _u32, _vp, _i, _u32,
                                       _vp, _f32, _vp, _sz, _vp]),
+    "b2sq_gemm_i8_host": (_i, [_u32, _u32, _u32, _vp, _vp, _vp, _vp, _f32, _f32, _vp, _i, _vp, _sz, _u32, _u32,
+                               _vp]),
+    "b2sq_gemm_i8_host_buffer_size": (_i, [_u32, _u32, _u32, _i, C.POINTER(_sz)]),
     "b2sq_gemm_i8_workspace_size": (_i, [_u32, _u32, _u32, _i, _i, C.POINTER(_sz)]),
     "b2sq_gemm_i8_plan": (_i, [_u32, _u32, _u32, _i, _i, _i, _u32, C.POINTER(GemmPlan)]),
     "b2sq_gemm_i8_allgather": (_i, [_u32, _u32, _u32, _vp, _i, _u32, _vp, _i, _u32, _vp, _u32, _u32, _u32, _i, _u32,

@@ -227,56 +227,47 @@ gemm_quant_tensor_scale = gemm_quant
 
 # ----------------------------------------------------------------------------- MoE
 class HostGemmBuffers:
-    """Device buffers and copy streams reused by gemm_quant_host (one per shape and device)."""
+    """The device buffer gemm_quant_host reuses (one per shape, dtype and device)."""
 
     def __init__(self, m: int, n: int, k: int, out_dtype: torch.dtype, device: torch.device):
         self.key = (m, n, k, out_dtype, device)
-        self.a = torch.empty((m, k), dtype=torch.int8, device=device)
-        self.w = torch.empty((n, k), dtype=torch.int8, device=device)
-        self.sa = torch.empty((m,), dtype=torch.float32, device=device)
-        self.sb = torch.empty((n,), dtype=torch.float32, device=device)
-        self.c = torch.empty((m, n), dtype=out_dtype, device=device)
-        self.s_in = torch.cuda.Stream(device)
-        self.s_out = torch.cuda.Stream(device)
+        lib = _lib.load()
+        size = C.c_size_t(0)
+        _lib.check(lib.b2sq_gemm_i8_host_buffer_size(m, n, k, _DTYPE_CODE[out_dtype], C.byref(size)),
+                   "b2sq_gemm_i8_host_buffer_size")
+        self.buf = torch.empty((size.value,), dtype=torch.uint8, device=device)
 
 
 def gemm_quant_host(h_a: torch.Tensor, h_w_nk: torch.Tensor, h_sa: torch.Tensor, h_sb: torch.Tensor,
-                    h_c: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16, chunks: int = 8,
+                    h_c: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16, chunks: int = 0,
                     buffers: Optional[HostGemmBuffers] = None, workspace: Optional[Workspace] = None,
-                    device: Optional[torch.device] = None) -> HostGemmBuffers:
-    """h_c = dequant(h_a @ h_w_nk.T) for operands and result in (pinned) host memory.
-
-    The weights and their scales are copied to the device once per call; the
-    activations go in `chunks` row blocks whose host->device copy, GEMM
-    (b2sq_gemm_i8 on the current stream) and device->host copy overlap on
-    three streams, so the transfer time is about one direction's bytes
-    instead of both directions' plus the GEMM.  On return the work is queued
-    on the current stream (synchronise it before reading h_c).  Returns the
-    device buffers, to pass back in on the next call."""
+                    device: Optional[torch.device] = None, col_chunks: Optional[int] = None) -> HostGemmBuffers:
+    """h_c = dequant(h_a @ h_w_nk.T) for operands and result in (pinned) host
+    memory, through b2sq_gemm_i8_host: the problem is cut into chunks x
+    col_chunks output blocks (0 = the library's choice) whose host->device
+    copies, GEMMs and device->host copies overlap.  On return the work is
+    queued on the current stream (synchronise it before reading h_c).
+    Returns the device buffer holder, to pass back in on the next call.
+    `workspace` is accepted for compatibility and unused (the block GEMMs need
+    none)."""
+    del workspace
+    for t, dt in ((h_a, torch.int8), (h_w_nk, torch.int8), (h_sa, torch.float32), (h_sb, torch.float32),
+                  (h_c, out_dtype)):
+        if t.device.type != "cpu" or t.dtype != dt or not t.is_contiguous():
+            raise ValueError("host operands: contiguous CPU tensors of the documented dtypes expected")
     M, K = h_a.shape
     N = h_w_nk.shape[0]
+    if h_w_nk.shape[1] != K or h_c.shape != (M, N) or h_sa.numel() != M or h_sb.numel() != N:
+        raise ValueError("shape mismatch among the host operands")
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
     key = (M, N, K, out_dtype, dev)
     b = buffers if buffers is not None and buffers.key == key else HostGemmBuffers(M, N, K, out_dtype, dev)
-    cur = torch.cuda.current_stream(dev)
-    b.s_in.wait_stream(cur)  # earlier work on these buffers is done before they are overwritten
-    b.s_out.wait_stream(cur)
-    with torch.cuda.stream(b.s_in):
-        b.w.copy_(h_w_nk, non_blocking=True)
-        b.sb.copy_(h_sb, non_blocking=True)
-    rows = (M + chunks - 1) // chunks
-    for r0 in range(0, M, rows):
-        r1 = min(M, r0 + rows)
-        with torch.cuda.stream(b.s_in):
-            b.a[r0:r1].copy_(h_a[r0:r1], non_blocking=True)
-            b.sa[r0:r1].copy_(h_sa[r0:r1], non_blocking=True)
-        cur.wait_stream(b.s_in)
-        gemm_quant(b.a[r0:r1], b.w.t(), b.sa[r0:r1], b.sb, out_dtype=out_dtype, c=b.c[r0:r1], workspace=workspace,
-                   stream=cur)
-        b.s_out.wait_stream(cur)
-        with torch.cuda.stream(b.s_out):
-            h_c[r0:r1].copy_(b.c[r0:r1], non_blocking=True)
-    cur.wait_stream(b.s_out)
+    lib = _lib.load()
+    st = lib.b2sq_gemm_i8_host(M, N, K, h_a.data_ptr(), h_w_nk.data_ptr(), h_sa.data_ptr(), h_sb.data_ptr(), 1.0,
+                               1.0, h_c.data_ptr(), _DTYPE_CODE[out_dtype], b.buf.data_ptr(), b.buf.numel(),
+                               int(chunks), int(chunks if col_chunks is None else col_chunks),
+                               _stream_ptr(None, dev))
+    _lib.check(st, "b2sq_gemm_i8_host")
     return b
 
 

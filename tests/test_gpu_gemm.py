@@ -187,7 +187,8 @@ def test_bounded_wait_reports_timeout(cuda_device):
     run_case(128, 256, 256)
 
 
-@pytest.mark.parametrize("M,N,K,chunks", [(1000, 512, 256, 3), (4096, 1024, 512, 8), (7, 256, 128, 4)])
+@pytest.mark.parametrize("M,N,K,chunks", [(1000, 512, 256, 3), (4096, 1024, 512, 8), (7, 256, 128, 4),
+                                          (3000, 2304, 256, 0), (8192, 8192, 256, 0)])
 def test_gemm_from_host_buffers(cuda_device, M, N, K, chunks):
     """gemm_quant_host (pinned host operands and result, chunked and overlapped)
     equals gemm_quant on device tensors, bit for bit, and reuses its buffers."""
