@@ -32,6 +32,7 @@
 //  * no TMA multicast anywhere (every CTA loads its own tiles).
 #include "common.cuh"
 #include "kernels.h"
+#include "sq_math.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -52,6 +53,10 @@ namespace {
 #endif
 
 constexpr uint32_t kThreads = 192;  // 6 warps
+// Decode GEMM with smoothquant fused in front: four more warps quantise the
+// activations straight into the B operand's shared-memory stages.
+constexpr uint32_t kQuantWarps = 4;
+constexpr uint32_t kThreadsSQ = kThreads + 32 * kQuantWarps;
 constexpr uint32_t kEpiThreads = 128;
 constexpr uint32_t kSmemBudget = 232448;  // 227 KiB opt-in limit per CTA
 constexpr uint32_t kBarrierBytes = 256;
@@ -101,6 +106,17 @@ struct KParams {
     // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
     // row scales) are written by the kernel launched just before this one.
     uint32_t pdl_dep;
+    // Fused smoothquant (decode): the kernel B operand is quantised in the
+    // kernel from fp16 activations sq_x [Nk rows, K] (row pitch sq_ldx
+    // elements) and smooth scales sq_s [K]; CTA 0 also writes the int8 rows
+    // to sq_xq_out [Nk, K] and the row scales to sq_rs_out [Nk] (each
+    // nullable).  The row scales are the kernel's column scales.
+    const uint16_t* sq_x;
+    uint32_t sq_ldx;
+    const float* sq_s;
+    float sq_qmax;
+    int8_t* sq_xq_out;
+    float* sq_rs_out;
 };
 
 constexpr uint32_t kTileK_Grouped = tile_k_for(256);
@@ -223,6 +239,11 @@ struct Smem {
     static constexpr uint32_t taddr_off = tempty_off + 16;
     static constexpr uint32_t abort_off = taddr_off + 4;
     static constexpr uint32_t flag_off = abort_off + 4;
+    // fused smoothquant: "row scales ready" mbarrier, row scales, reciprocals
+    static constexpr uint32_t sqbar_off = (flag_off + 4 + 7) & ~7u;
+    static constexpr uint32_t sqrs_off = sqbar_off + 8;
+    static constexpr uint32_t sqinv_off = sqrs_off + 4 * BN;
+    static constexpr bool sq_fits = sqinv_off + 4 * BN <= bar_off + kBarrierBytes;
     // 4 KiB per epilogue warp to re-shape output chunks for coalesced stores
     // to peer GPUs (all-gather), when the pipeline leaves room for it.
     static constexpr uint32_t epi_off = bar_off + kBarrierBytes;
@@ -503,12 +524,13 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
     store_chunk<W, G>(p, row, col0 + W, a1, rsc, cs1);
 }
 
-template <uint32_t BN, uint32_t BK, bool kGrouped, bool G = false>
-__global__ void __launch_bounds__(kThreads, 1)
+template <uint32_t BN, uint32_t BK, bool kGrouped, bool G = false, bool kSQ = false>
+__global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p,
                    uint64_t wait_limit_ns)
 {
     using L = Smem<BN, BK, G>;
+    static_assert(!kSQ || (L::sq_fits && !kGrouped && !G), "fused smoothquant: decode tiles only");
     constexpr uint32_t ST = L::ST;
     constexpr uint32_t TMEM_COLS = tmem_cols(BN);
     constexpr uint32_t CW = BN < 32 ? BN : 32;  // columns per tcgen05.ld
@@ -530,15 +552,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
 
+    const uint32_t sq_bar = sbase + L::sqbar_off;
+    volatile float* s_rs = reinterpret_cast<volatile float*>(smem + L::sqrs_off);
+    volatile float* s_inv = reinterpret_cast<volatile float*>(smem + L::sqinv_off);
+
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < ST; ++s) {
-            mbar_init(full_bar + 8 * s, 1);
+            // fused smoothquant: a stage is full once its A bytes have landed
+            // and every quantising warp has written its share of B
+            mbar_init(full_bar + 8 * s, kSQ ? 1 + kQuantWarps : 1);
             mbar_init(empty_bar + 8 * s, 1);
         }
         for (uint32_t b = 0; b < 2; ++b) {
             mbar_init(tfull_bar + 8 * b, 1);
             mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
         }
+        if constexpr (kSQ) mbar_init(sq_bar, kQuantWarps);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
@@ -573,6 +602,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
+            // fused smoothquant: launched with PDL, so nothing global is read
+            // before the previous kernel of the stream has completed
+            if constexpr (kSQ) griddep_wait();
             UnitIter it;
             it.init(p, tiles_total);
             Unit u;
@@ -633,10 +665,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = full_bar + 8 * stage;
-                    mbar_arrive_expect_tx(fb, L::SB);
+                    mbar_arrive_expect_tx(fb, kSQ ? L::A_BYTES : L::SB);
                     const uint32_t sa = sbase + stage * L::SB;
                     const uint32_t sb = sa + L::A_BYTES;
-                    if (!pdl_pending) {
+                    if constexpr (kSQ) {
+                        load_a(sa, fb, kb, a_row);  // B is written by the quantising warps
+                    } else if (!pdl_pending) {
                         load_a(sa, fb, kb, a_row);
                         load_b(sb, fb, kb, b_row);
                     } else {
@@ -706,9 +740,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();  // reconverge before the CTA-wide barrier below
-    } else {
+    } else if (!kSQ || warp < 6) {
         // ------------------------------------------------------------ epilogue
         if (p.pdl_dep) griddep_wait();  // row scales come from the previous kernel
+        bool scales_ok = true;
+        if constexpr (kSQ) {
+            griddep_wait();
+            // the column scales are the token row scales the quantising warps compute
+            scales_ok = mbar_wait(sq_bar, 0, SITE_FUSED_SCALES, abort_flag, wait_limit_ns);
+        }
         const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
         const uint32_t row_local = q * 32 + lane;
         const uint32_t epi_stage = L::EPI ? sbase + L::epi_off + q * 4096 : 0u;
@@ -717,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         it.init(p, tiles_total);
         Unit u;
         uint32_t uidx = 0;
-        bool ok = true;
+        bool ok = scales_ok;
         while (ok && it.next(p, u)) {
             const uint32_t buf = uidx & 1;
             const uint32_t use = uidx >> 1;
@@ -740,8 +780,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ++ch) {
                 const uint32_t col = tn_col0 + ch * CW + (lane % CW);
-                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f)
-                                          : p.col_scale;
+                if constexpr (kSQ) csv[ch] = col < p.Nk ? s_rs[col] : 0.f;
+                else csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f)
+                                               : p.col_scale;
             }
             if (full) {
                 if constexpr (NCH == 1) {
@@ -824,6 +865,96 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             ++uidx;
+        }
+    } else {
+        // ------------------------------------------------------------ quantising warps (fused smoothquant)
+        if constexpr (kSQ) {
+            griddep_wait();
+            const uint32_t qt = threadIdx.x - kThreads;  // 0 .. 32 * kQuantWarps - 1
+            const uint32_t qw = qt >> 5;
+            const float qmax = p.sq_qmax;
+            const bool integral = qmax == truncf(qmax);
+            const uint32_t nvec = p.K / 8;
+            // Pass 1: each token row's absmax of x * s over all of K (reference :83-96).
+            for (uint32_t r = qw; r < BN; r += kQuantWarps) {
+                float amax = 0.f;
+                if (r < p.Nk) {
+                    const uint16_t* xr = p.sq_x + (size_t)r * p.sq_ldx;
+                    for (uint32_t v = lane; v < nvec; v += 32) {
+                        float xf[8];
+                        unpack8(__ldg(reinterpret_cast<const uint4*>(xr + (size_t)v * 8)), xf);
+                        const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8));
+                        const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8) + 1);
+                        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__fmul_rn(xf[i], sv[i])));
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+                if (lane == 0) {
+                    const float rs = row_scale_of(amax, qmax);
+                    s_rs[r] = rs;
+                    s_inv[r] = inv_scale_of(rs);
+                    if (blockIdx.x == 0 && p.sq_rs_out != nullptr && r < p.Nk) p.sq_rs_out[r] = rs;
+                }
+            }
+            named_bar_sync(2, 32 * kQuantWarps);  // every row's scale is in shared memory
+            if (lane == 0) mbar_arrive(sq_bar);   // the epilogue may read them
+            // Pass 2: quantise each stage's K slice straight into the B tile,
+            // in the 128-byte-swizzled K-major layout a TMA load would give
+            // (row r of an atom at r * 128, its 16-byte piece c at c ^ (r % 8)).
+            constexpr uint32_t CPR = BK / 16;  // 16-byte pieces per row per stage
+            UnitIter it;
+            it.init(p, tiles_total);
+            Unit u;
+            uint32_t stage = 0, phase = 0;
+            bool ok = true, first_unit = true;
+            while (ok && it.next(p, u)) {
+                for (uint32_t kb = u.k0; kb < u.k1; ++kb) {
+                    if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_FUSED_QUANT, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sbB = sbase + stage * L::SB + L::A_BYTES;
+                    for (uint32_t item = qt; item < BN * CPR; item += 32 * kQuantWarps) {
+                        const uint32_t r = item / CPR, c = item % CPR;
+                        const uint32_t k0 = kb * BK + c * 16;
+                        uint32_t w[4] = {0u, 0u, 0u, 0u};
+                        if (r < p.Nk && k0 < p.K) {
+                            const uint16_t* xp = p.sq_x + (size_t)r * p.sq_ldx + k0;
+                            const float inv = s_inv[r];
+#pragma unroll
+                            for (uint32_t h = 0; h < 2; ++h) {
+                                float xf[8];
+                                unpack8(__ldg(reinterpret_cast<const uint4*>(xp) + h), xf);
+                                const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + k0 + 8 * h));
+                                const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + k0 + 8 * h) + 1);
+                                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                                uint32_t b[8];
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    const float xs = __fmul_rn(xf[i], sv[i]);
+                                    b[i] = integral ? quant_bits(xs, inv, qmax) : (uint32_t)(uint8_t)quant1(xs, inv, qmax);
+                                }
+                                w[2 * h] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+                                w[2 * h + 1] = pack_low_bytes(b[4], b[5], b[6], b[7]);
+                            }
+                            if (first_unit && blockIdx.x == 0 && p.sq_xq_out != nullptr)
+                                *reinterpret_cast<uint4*>(p.sq_xq_out + (size_t)r * p.K + k0) =
+                                    make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                        sts128(sbB + (c / 8) * (BN * 128) + r * 128 + (((c % 8) ^ (r & 7)) << 4), w[0], w[1], w[2],
+                               w[3]);
+                    }
+                    fence_async_smem();  // the tensor core reads the tile through the async proxy
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(full_bar + 8 * stage);
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+                first_unit = false;
+            }
+            __syncwarp();
         }
     }
 
@@ -1142,10 +1273,11 @@ bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint3
     return r == CUDA_SUCCESS;
 }
 
-template <uint32_t BN, uint32_t BK, bool kGrouped = false, bool G = false>
+template <uint32_t BN, uint32_t BK, bool kGrouped = false, bool G = false, bool kSQ = false>
 cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
     using L = Smem<BN, BK, G>;
+    constexpr uint32_t threads = kSQ ? kThreadsSQ : kThreads;
     // The shared-memory opt-in is a per-device function attribute.
     static std::atomic<uint64_t> done_mask{0};
     int dev = 0;
@@ -1153,15 +1285,18 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 L::total);
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped, G, kSQ>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    if (kp.pdl_dep) {
+    // The fused smoothquant kernel is always launched with PDL: every role
+    // waits for the previous kernel before touching global memory, so only
+    // its set-up overlaps the previous kernel's tail.
+    if (kp.pdl_dep || kSQ) {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(kp.ctas);
-        cfg.blockDim = dim3(kThreads);
+        cfg.blockDim = dim3(threads);
         cfg.dynamicSmemBytes = L::total;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
@@ -1169,9 +1304,9 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped, G>, ta, tb, kp, (uint64_t)kWaitLimitNs);
+        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped, G, kSQ>, ta, tb, kp, (uint64_t)kWaitLimitNs);
     }
-    gemm_i8_kernel<BN, BK, kGrouped, G><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_kernel<BN, BK, kGrouped, G, kSQ><<<kp.ctas, threads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -1326,6 +1461,23 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.raster_group = B2SQ_RASTER_GROUP;
     kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
+    if (p.sq_x != nullptr) {
+        // smoothquant fused into the decode GEMM (16-wide token tiles, whole tiles only)
+        if (bn != 16 || s.cta_pair || s.sk_iters != 0 || s.tile_k != tile_k_for(16) || !p.transpose_out ||
+            p.b_mn_major || p.n_extra || p.mc_c) {
+            if (detail) *detail = "internal: fused smoothquant needs the swapped 16-wide decode schedule";
+            return cudaErrorInvalidValue;
+        }
+        kp.sq_x = static_cast<const uint16_t*>(p.sq_x);
+        kp.sq_ldx = p.sq_ldx;
+        kp.sq_s = p.sq_s;
+        kp.sq_qmax = p.sq_qmax;
+        kp.sq_xq_out = p.sq_xq;
+        kp.sq_rs_out = p.sq_rs;
+        kp.col_scale_vec = nullptr;
+        kp.pdl_dep = 0;
+        return launch_tile<16, tile_k_for(16), false, false, true>(ta, tb, kp, st);
+    }
     // The all-gather epilogue (extra destinations / multicast) is a separate
     // build of each kernel, so plain GEMMs carry none of its code.
     const bool gather = p.n_extra > 0 || p.mc_c != nullptr;

@@ -76,3 +76,36 @@ def test_fused_decode_replays_in_a_cuda_graph(cuda_device):
         ref, _, _ = api.smoothquant_gemm(x, s, w, sb, out_dtype=torch.float16, workspace=ws)
         torch.cuda.synchronize()
         assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("M,K,N,qmax", [(16, 1040, 4096, 127.0), (3, 8192, 28672, 127.0), (11, 4112, 2304, 100.5),
+                                        (16, 2048, 512, 7.0), (1, 16, 256, 127.0)])
+def test_single_kernel_decode_matches_two_calls(cuda_device, M, K, N, qmax):
+    """Decode sizes (M <= 16, K-major weights) run as ONE kernel that
+    quantises the tokens into its own shared-memory operand tiles: Xq, row
+    scales and the fp16 output are bit-identical to b2sq_smoothquant followed
+    by b2sq_gemm_i8, including ragged K, fractional quant_max and rows with
+    inf / NaN / all-zero inputs."""
+    dev = cuda_device
+    rng = np.random.default_rng(M * 7 + K)
+    xn = synth.activations_np(rng, M, K, 4, 30.0)
+    if M >= 3:
+        xn[0, K // 3] = np.inf
+        xn[1, :] = 0
+        xn[2, 5] = np.nan
+    x = torch.from_numpy(xn).to(dev)
+    s = torch.from_numpy(synth.smooth_np(rng, K)).to(dev)
+    w = synth.torch_int8_uniform((N, K), dev, 9)
+    sb = synth.torch_scales(N, dev, 10)
+    for rep in range(2):
+        c, xq, rs = api.smoothquant_gemm(x, s, w, sb, quant_max=qmax, out_dtype=torch.float16)
+        y2, rs2 = api.smoothquant(x, s, quant_max=qmax)
+        c2 = api.gemm_quant(y2, w.t(), rs2, sb, out_dtype=torch.float16)
+        torch.cuda.synchronize()
+        assert torch.equal(xq, y2)
+        assert torch.equal(rs.view(torch.int32), rs2.view(torch.int32)) or \
+            bool(((rs == rs2) | (torch.isnan(rs) & torch.isnan(rs2))).all())
+        assert torch.equal(c.view(torch.int16), c2.view(torch.int16))
+    y0, r0 = O.smoothquant(xn, s.cpu().numpy(), qmax)
+    assert np.array_equal(xq.cpu().numpy(), y0)
+    assert api.last_device_error() == 0
