@@ -461,7 +461,7 @@ def n1_sections(args, dev, api, synth, timed, l2_flush, stream, hbm_gbs, ws):
         bytes_d = (md * K * 2 + md * K + K * 4 + md * 4) + (md * K + 28672 * K + 4 * 28672 + 4 * md + 2 * md * 28672)
         decode[f"m{md}"] = {"ms": r4(ms_d), "gbs": r4(bytes_d / (ms_d * 1e-3) / 1e9),
                             "frac_of_measured_hbm": r4(bytes_d / (ms_d * 1e-3) / 1e9 / hbm_gbs),
-                            "shape": [md, K, 28672], "gpu_launches_per_step": 2}
+                            "shape": [md, K, 28672], "gpu_launches_per_step": 1 if md <= 16 else 2}
     out["decode"] = decode
     del w_dec
 

@@ -55,7 +55,7 @@ namespace {
 constexpr uint32_t kThreads = 192;  // 6 warps
 // Decode GEMM with smoothquant fused in front: four more warps quantise the
 // activations straight into the B operand's shared-memory stages.
-constexpr uint32_t kQuantWarps = 4;
+constexpr uint32_t kQuantWarps = 8;
 constexpr uint32_t kThreadsSQ = kThreads + 32 * kQuantWarps;
 constexpr uint32_t kEpiThreads = 128;
 constexpr uint32_t kSmemBudget = 232448;  // 227 KiB opt-in limit per CTA
@@ -567,7 +567,10 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
             mbar_init(tfull_bar + 8 * b, 1);
             mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
         }
-        if constexpr (kSQ) mbar_init(sq_bar, kQuantWarps);
+        if constexpr (kSQ) {
+            mbar_init(sq_bar, kQuantWarps);
+            for (uint32_t r = 0; r < BN; ++r) s_inv[r] = 0.f;  // row maxima accumulate here
+        }
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
@@ -875,29 +878,47 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
             const float qmax = p.sq_qmax;
             const bool integral = qmax == truncf(qmax);
             const uint32_t nvec = p.K / 8;
-            // Pass 1: each token row's absmax of x * s over all of K (reference :83-96).
-            for (uint32_t r = qw; r < BN; r += kQuantWarps) {
-                float amax = 0.f;
-                if (r < p.Nk) {
-                    const uint16_t* xr = p.sq_x + (size_t)r * p.sq_ldx;
-                    for (uint32_t v = lane; v < nvec; v += 32) {
-                        float xf[8];
-                        unpack8(__ldg(reinterpret_cast<const uint4*>(xr + (size_t)v * 8)), xf);
-                        const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8));
-                        const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8) + 1);
-                        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            constexpr uint32_t QT = 32 * kQuantWarps;
+            // Pass 1: each token row's absmax of x * s over all of K (reference
+            // :83-96).  A thread takes one 8-element column vector of every row
+            // at a time, so all its loads for that vector are in flight at once
+            // (the latency of these L2 reads, not their bytes, is the cost).
+            float amax[BN];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__fmul_rn(xf[i], sv[i])));
-                    }
-                }
+            for (uint32_t r = 0; r < BN; ++r) amax[r] = 0.f;
+            for (uint32_t v = qt; v < nvec; v += QT) {
+                const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8));
+                const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8) + 1);
+                uint4 raw[BN];
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-                if (lane == 0) {
-                    const float rs = row_scale_of(amax, qmax);
-                    s_rs[r] = rs;
-                    s_inv[r] = inv_scale_of(rs);
-                    if (blockIdx.x == 0 && p.sq_rs_out != nullptr && r < p.Nk) p.sq_rs_out[r] = rs;
+                for (uint32_t r = 0; r < BN; ++r)
+                    raw[r] = r < p.Nk ? __ldg(reinterpret_cast<const uint4*>(p.sq_x + (size_t)r * p.sq_ldx) + v)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                for (uint32_t r = 0; r < BN; ++r) {
+                    float xf[8];
+                    unpack8(raw[r], xf);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) amax[r] = fmaxf(amax[r], fabsf(__fmul_rn(xf[i], sv[i])));
                 }
+            }
+            // Block-wide max per row: warp shuffles, then an integer atomicMax in
+            // shared memory (amax >= 0 and never NaN, so its bits order like ints);
+            // s_inv holds the maxima until the scales replace them.
+#pragma unroll
+            for (uint32_t r = 0; r < BN; ++r) {
+                float m = amax[r];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+                if (lane == 0) atomicMax(reinterpret_cast<int*>(const_cast<float*>(s_inv + r)), __float_as_int(m));
+            }
+            named_bar_sync(2, QT);
+            if (qt < BN) {
+                const float rs = row_scale_of(s_inv[qt], qmax);
+                s_rs[qt] = rs;
+                s_inv[qt] = inv_scale_of(rs);
+                if (blockIdx.x == 0 && p.sq_rs_out != nullptr && qt < p.Nk) p.sq_rs_out[qt] = rs;
             }
             named_bar_sync(2, 32 * kQuantWarps);  // every row's scale is in shared memory
             if (lane == 0) mbar_arrive(sq_bar);   // the epilogue may read them
@@ -917,19 +938,38 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
                         break;
                     }
                     const uint32_t sbB = sbase + stage * L::SB + L::A_BYTES;
-                    for (uint32_t item = qt; item < BN * CPR; item += 32 * kQuantWarps) {
+                    // every load of this thread's pieces first, then the arithmetic and the stores
+                    constexpr uint32_t IPT = (BN * CPR + QT - 1) / QT;  // pieces per thread
+                    uint4 raw[IPT][2];
+                    float4 sc[IPT][4];
+#pragma unroll
+                    for (uint32_t t = 0; t < IPT; ++t) {
+                        const uint32_t item = qt + t * QT;
+                        const uint32_t r = item / CPR, c = item % CPR;
+                        const uint32_t k0 = kb * BK + c * 16;
+                        const bool live = item < BN * CPR && r < p.Nk && k0 < p.K;
+                        const uint4* xp = reinterpret_cast<const uint4*>(p.sq_x + (size_t)(live ? r : 0) * p.sq_ldx +
+                                                                         (live ? k0 : 0));
+                        const float4* sp = reinterpret_cast<const float4*>(p.sq_s + (live ? k0 : 0));
+                        raw[t][0] = live ? __ldg(xp) : make_uint4(0u, 0u, 0u, 0u);
+                        raw[t][1] = live ? __ldg(xp + 1) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                        for (uint32_t h = 0; h < 4; ++h) sc[t][h] = live ? __ldg(sp + h) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (uint32_t t = 0; t < IPT; ++t) {
+                        const uint32_t item = qt + t * QT;
+                        if (item >= BN * CPR) break;
                         const uint32_t r = item / CPR, c = item % CPR;
                         const uint32_t k0 = kb * BK + c * 16;
                         uint32_t w[4] = {0u, 0u, 0u, 0u};
                         if (r < p.Nk && k0 < p.K) {
-                            const uint16_t* xp = p.sq_x + (size_t)r * p.sq_ldx + k0;
                             const float inv = s_inv[r];
 #pragma unroll
                             for (uint32_t h = 0; h < 2; ++h) {
                                 float xf[8];
-                                unpack8(__ldg(reinterpret_cast<const uint4*>(xp) + h), xf);
-                                const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + k0 + 8 * h));
-                                const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + k0 + 8 * h) + 1);
+                                unpack8(raw[t][h], xf);
+                                const float4 s0 = sc[t][2 * h], s1 = sc[t][2 * h + 1];
                                 const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
                                 uint32_t b[8];
 #pragma unroll
