@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64"], default=None,
+    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64", "fused16"], default=None,
                     help="run 3 launches of one kernel on its workload and exit (for ncu captures)")
     return ap.parse_args()
 
@@ -79,6 +79,13 @@ def run_profile(kind: str):
         s = torch.ones((SQ_K,), device=dev)
         for _ in range(3):
             api.smoothquant(x, s)
+    elif kind == "fused16":  # config 3, M = 16: smoothquant inside the decode GEMM
+        x = torch.randn((16, K), device=dev).to(torch.float16)
+        s = torch.empty((K,), device=dev).uniform_(0.5, 2.0)
+        w = synth.torch_int8_uniform((28672, K), dev, 2)
+        sb = synth.torch_scales(28672, dev, 4)
+        for _ in range(3):
+            api.smoothquant_gemm(x, s, w, sb, out_dtype=torch.float16)
     else:
         m = {"gemm": M, "decode16": 16, "decode64": 64}[kind]
         n = N if kind == "gemm" else 28672

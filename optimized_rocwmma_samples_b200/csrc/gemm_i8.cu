@@ -53,10 +53,6 @@ namespace {
 #endif
 
 constexpr uint32_t kThreads = 192;  // 6 warps
-// Decode GEMM with smoothquant fused in front: four more warps quantise the
-// activations straight into the B operand's shared-memory stages.
-constexpr uint32_t kQuantWarps = 8;
-constexpr uint32_t kThreadsSQ = kThreads + 32 * kQuantWarps;
 constexpr uint32_t kEpiThreads = 128;
 constexpr uint32_t kSmemBudget = 232448;  // 227 KiB opt-in limit per CTA
 constexpr uint32_t kBarrierBytes = 256;
@@ -106,11 +102,11 @@ struct KParams {
     // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
     // row scales) are written by the kernel launched just before this one.
     uint32_t pdl_dep;
-    // Fused smoothquant (decode): the kernel B operand is quantised in the
-    // kernel from fp16 activations sq_x [Nk rows, K] (row pitch sq_ldx
-    // elements) and smooth scales sq_s [K]; CTA 0 also writes the int8 rows
-    // to sq_xq_out [Nk, K] and the row scales to sq_rs_out [Nk] (each
-    // nullable).  The row scales are the kernel's column scales.
+    // Decode GEMM with smoothquant fused in front (gemm_i8_decode_sq_kernel):
+    // the token operand is quantised in the kernel from fp16 sq_x [Nk, K]
+    // (pitch sq_ldx elements) and smooth scales sq_s [K]; CTA 0 also writes
+    // the int8 rows to sq_xq_out [Nk, K] and the row scales to sq_rs_out [Nk]
+    // (each nullable).  The row scales are the kernel's column scales.
     const uint16_t* sq_x;
     uint32_t sq_ldx;
     const float* sq_s;
@@ -239,11 +235,6 @@ struct Smem {
     static constexpr uint32_t taddr_off = tempty_off + 16;
     static constexpr uint32_t abort_off = taddr_off + 4;
     static constexpr uint32_t flag_off = abort_off + 4;
-    // fused smoothquant: "row scales ready" mbarrier, row scales, reciprocals
-    static constexpr uint32_t sqbar_off = (flag_off + 4 + 7) & ~7u;
-    static constexpr uint32_t sqrs_off = sqbar_off + 8;
-    static constexpr uint32_t sqinv_off = sqrs_off + 4 * BN;
-    static constexpr bool sq_fits = sqinv_off + 4 * BN <= bar_off + kBarrierBytes;
     // 4 KiB per epilogue warp to re-shape output chunks for coalesced stores
     // to peer GPUs (all-gather), when the pipeline leaves room for it.
     static constexpr uint32_t epi_off = bar_off + kBarrierBytes;
@@ -524,13 +515,12 @@ __device__ __forceinline__ void store_pair(const KParams& p, uint32_t row, uint3
     store_chunk<W, G>(p, row, col0 + W, a1, rsc, cs1);
 }
 
-template <uint32_t BN, uint32_t BK, bool kGrouped, bool G = false, bool kSQ = false>
-__global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
+template <uint32_t BN, uint32_t BK, bool kGrouped, bool G = false>
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const KParams p,
                    uint64_t wait_limit_ns)
 {
     using L = Smem<BN, BK, G>;
-    static_assert(!kSQ || (L::sq_fits && !kGrouped && !G), "fused smoothquant: decode tiles only");
     constexpr uint32_t ST = L::ST;
     constexpr uint32_t TMEM_COLS = tmem_cols(BN);
     constexpr uint32_t CW = BN < 32 ? BN : 32;  // columns per tcgen05.ld
@@ -552,24 +542,14 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
 
-    const uint32_t sq_bar = sbase + L::sqbar_off;
-    volatile float* s_rs = reinterpret_cast<volatile float*>(smem + L::sqrs_off);
-    volatile float* s_inv = reinterpret_cast<volatile float*>(smem + L::sqinv_off);
-
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < ST; ++s) {
-            // fused smoothquant: a stage is full once its A bytes have landed
-            // and every quantising warp has written its share of B
-            mbar_init(full_bar + 8 * s, kSQ ? 1 + kQuantWarps : 1);
+            mbar_init(full_bar + 8 * s, 1);
             mbar_init(empty_bar + 8 * s, 1);
         }
         for (uint32_t b = 0; b < 2; ++b) {
             mbar_init(tfull_bar + 8 * b, 1);
             mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
-        }
-        if constexpr (kSQ) {
-            mbar_init(sq_bar, kQuantWarps);
-            for (uint32_t r = 0; r < BN; ++r) s_inv[r] = 0.f;  // row maxima accumulate here
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -605,9 +585,6 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            // fused smoothquant: launched with PDL, so nothing global is read
-            // before the previous kernel of the stream has completed
-            if constexpr (kSQ) griddep_wait();
             UnitIter it;
             it.init(p, tiles_total);
             Unit u;
@@ -668,12 +645,10 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
                         break;
                     }
                     const uint32_t fb = full_bar + 8 * stage;
-                    mbar_arrive_expect_tx(fb, kSQ ? L::A_BYTES : L::SB);
+                    mbar_arrive_expect_tx(fb, L::SB);
                     const uint32_t sa = sbase + stage * L::SB;
                     const uint32_t sb = sa + L::A_BYTES;
-                    if constexpr (kSQ) {
-                        load_a(sa, fb, kb, a_row);  // B is written by the quantising warps
-                    } else if (!pdl_pending) {
+                    if (!pdl_pending) {
                         load_a(sa, fb, kb, a_row);
                         load_b(sb, fb, kb, b_row);
                     } else {
@@ -743,15 +718,9 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
             }
         }
         __syncwarp();  // reconverge before the CTA-wide barrier below
-    } else if (!kSQ || warp < 6) {
+    } else {
         // ------------------------------------------------------------ epilogue
         if (p.pdl_dep) griddep_wait();  // row scales come from the previous kernel
-        bool scales_ok = true;
-        if constexpr (kSQ) {
-            griddep_wait();
-            // the column scales are the token row scales the quantising warps compute
-            scales_ok = mbar_wait(sq_bar, 0, SITE_FUSED_SCALES, abort_flag, wait_limit_ns);
-        }
         const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
         const uint32_t row_local = q * 32 + lane;
         const uint32_t epi_stage = L::EPI ? sbase + L::epi_off + q * 4096 : 0u;
@@ -760,7 +729,7 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
         it.init(p, tiles_total);
         Unit u;
         uint32_t uidx = 0;
-        bool ok = scales_ok;
+        bool ok = true;
         while (ok && it.next(p, u)) {
             const uint32_t buf = uidx & 1;
             const uint32_t use = uidx >> 1;
@@ -783,9 +752,8 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ++ch) {
                 const uint32_t col = tn_col0 + ch * CW + (lane % CW);
-                if constexpr (kSQ) csv[ch] = col < p.Nk ? s_rs[col] : 0.f;
-                else csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f)
-                                               : p.col_scale;
+                csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f)
+                                          : p.col_scale;
             }
             if (full) {
                 if constexpr (NCH == 1) {
@@ -868,133 +836,6 @@ __global__ void __launch_bounds__(kSQ ? kThreadsSQ : kThreads, 1)
                 }
             }
             ++uidx;
-        }
-    } else {
-        // ------------------------------------------------------------ quantising warps (fused smoothquant)
-        if constexpr (kSQ) {
-            griddep_wait();
-            const uint32_t qt = threadIdx.x - kThreads;  // 0 .. 32 * kQuantWarps - 1
-            const uint32_t qw = qt >> 5;
-            const float qmax = p.sq_qmax;
-            const bool integral = qmax == truncf(qmax);
-            const uint32_t nvec = p.K / 8;
-            constexpr uint32_t QT = 32 * kQuantWarps;
-            // Pass 1: each token row's absmax of x * s over all of K (reference
-            // :83-96).  A thread takes one 8-element column vector of every row
-            // at a time, so all its loads for that vector are in flight at once
-            // (the latency of these L2 reads, not their bytes, is the cost).
-            float amax[BN];
-#pragma unroll
-            for (uint32_t r = 0; r < BN; ++r) amax[r] = 0.f;
-            for (uint32_t v = qt; v < nvec; v += QT) {
-                const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8));
-                const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8) + 1);
-                uint4 raw[BN];
-#pragma unroll
-                for (uint32_t r = 0; r < BN; ++r)
-                    raw[r] = r < p.Nk ? __ldg(reinterpret_cast<const uint4*>(p.sq_x + (size_t)r * p.sq_ldx) + v)
-                                      : make_uint4(0u, 0u, 0u, 0u);
-                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-                for (uint32_t r = 0; r < BN; ++r) {
-                    float xf[8];
-                    unpack8(raw[r], xf);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) amax[r] = fmaxf(amax[r], fabsf(__fmul_rn(xf[i], sv[i])));
-                }
-            }
-            // Block-wide max per row: warp shuffles, then an integer atomicMax in
-            // shared memory (amax >= 0 and never NaN, so its bits order like ints);
-            // s_inv holds the maxima until the scales replace them.
-#pragma unroll
-            for (uint32_t r = 0; r < BN; ++r) {
-                float m = amax[r];
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-                if (lane == 0) atomicMax(reinterpret_cast<int*>(const_cast<float*>(s_inv + r)), __float_as_int(m));
-            }
-            named_bar_sync(2, QT);
-            if (qt < BN) {
-                const float rs = row_scale_of(s_inv[qt], qmax);
-                s_rs[qt] = rs;
-                s_inv[qt] = inv_scale_of(rs);
-                if (blockIdx.x == 0 && p.sq_rs_out != nullptr && qt < p.Nk) p.sq_rs_out[qt] = rs;
-            }
-            named_bar_sync(2, 32 * kQuantWarps);  // every row's scale is in shared memory
-            if (lane == 0) mbar_arrive(sq_bar);   // the epilogue may read them
-            // Pass 2: quantise each stage's K slice straight into the B tile,
-            // in the 128-byte-swizzled K-major layout a TMA load would give
-            // (row r of an atom at r * 128, its 16-byte piece c at c ^ (r % 8)).
-            constexpr uint32_t CPR = BK / 16;  // 16-byte pieces per row per stage
-            UnitIter it;
-            it.init(p, tiles_total);
-            Unit u;
-            uint32_t stage = 0, phase = 0;
-            bool ok = true, first_unit = true;
-            while (ok && it.next(p, u)) {
-                for (uint32_t kb = u.k0; kb < u.k1; ++kb) {
-                    if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_FUSED_QUANT, abort_flag, wait_limit_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t sbB = sbase + stage * L::SB + L::A_BYTES;
-                    // every load of this thread's pieces first, then the arithmetic and the stores
-                    constexpr uint32_t IPT = (BN * CPR + QT - 1) / QT;  // pieces per thread
-                    uint4 raw[IPT][2];
-                    float4 sc[IPT][4];
-#pragma unroll
-                    for (uint32_t t = 0; t < IPT; ++t) {
-                        const uint32_t item = qt + t * QT;
-                        const uint32_t r = item / CPR, c = item % CPR;
-                        const uint32_t k0 = kb * BK + c * 16;
-                        const bool live = item < BN * CPR && r < p.Nk && k0 < p.K;
-                        const uint4* xp = reinterpret_cast<const uint4*>(p.sq_x + (size_t)(live ? r : 0) * p.sq_ldx +
-                                                                         (live ? k0 : 0));
-                        const float4* sp = reinterpret_cast<const float4*>(p.sq_s + (live ? k0 : 0));
-                        raw[t][0] = live ? __ldg(xp) : make_uint4(0u, 0u, 0u, 0u);
-                        raw[t][1] = live ? __ldg(xp + 1) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                        for (uint32_t h = 0; h < 4; ++h) sc[t][h] = live ? __ldg(sp + h) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-#pragma unroll
-                    for (uint32_t t = 0; t < IPT; ++t) {
-                        const uint32_t item = qt + t * QT;
-                        if (item >= BN * CPR) break;
-                        const uint32_t r = item / CPR, c = item % CPR;
-                        const uint32_t k0 = kb * BK + c * 16;
-                        uint32_t w[4] = {0u, 0u, 0u, 0u};
-                        if (r < p.Nk && k0 < p.K) {
-                            const float inv = s_inv[r];
-#pragma unroll
-                            for (uint32_t h = 0; h < 2; ++h) {
-                                float xf[8];
-                                unpack8(raw[t][h], xf);
-                                const float4 s0 = sc[t][2 * h], s1 = sc[t][2 * h + 1];
-                                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-                                uint32_t b[8];
-#pragma unroll
-                                for (int i = 0; i < 8; ++i) {
-                                    const float xs = __fmul_rn(xf[i], sv[i]);
-                                    b[i] = integral ? quant_bits(xs, inv, qmax) : (uint32_t)(uint8_t)quant1(xs, inv, qmax);
-                                }
-                                w[2 * h] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-                                w[2 * h + 1] = pack_low_bytes(b[4], b[5], b[6], b[7]);
-                            }
-                            if (first_unit && blockIdx.x == 0 && p.sq_xq_out != nullptr)
-                                *reinterpret_cast<uint4*>(p.sq_xq_out + (size_t)r * p.K + k0) =
-                                    make_uint4(w[0], w[1], w[2], w[3]);
-                        }
-                        sts128(sbB + (c / 8) * (BN * 128) + r * 128 + (((c % 8) ^ (r & 7)) << 4), w[0], w[1], w[2],
-                               w[3]);
-                    }
-                    fence_async_smem();  // the tensor core reads the tile through the async proxy
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(full_bar + 8 * stage);
-                    if (++stage == ST) stage = 0, phase ^= 1;
-                }
-                first_unit = false;
-            }
-            __syncwarp();
         }
     }
 
@@ -1313,11 +1154,10 @@ bool make_operand_map(CUtensorMap* map, const int8_t* base, uint32_t rows, uint3
     return r == CUDA_SUCCESS;
 }
 
-template <uint32_t BN, uint32_t BK, bool kGrouped = false, bool G = false, bool kSQ = false>
+template <uint32_t BN, uint32_t BK, bool kGrouped = false, bool G = false>
 cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, cudaStream_t st)
 {
     using L = Smem<BN, BK, G>;
-    constexpr uint32_t threads = kSQ ? kThreadsSQ : kThreads;
     // The shared-memory opt-in is a per-device function attribute.
     static std::atomic<uint64_t> done_mask{0};
     int dev = 0;
@@ -1325,18 +1165,15 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped, G, kSQ>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, BK, kGrouped, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 L::total);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    // The fused smoothquant kernel is always launched with PDL: every role
-    // waits for the previous kernel before touching global memory, so only
-    // its set-up overlaps the previous kernel's tail.
-    if (kp.pdl_dep || kSQ) {
+    if (kp.pdl_dep) {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(kp.ctas);
-        cfg.blockDim = dim3(threads);
+        cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = L::total;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
@@ -1344,9 +1181,9 @@ cudaError_t launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KPar
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped, G, kSQ>, ta, tb, kp, (uint64_t)kWaitLimitNs);
+        return cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, BK, kGrouped, G>, ta, tb, kp, (uint64_t)kWaitLimitNs);
     }
-    gemm_i8_kernel<BN, BK, kGrouped, G, kSQ><<<kp.ctas, threads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
+    gemm_i8_kernel<BN, BK, kGrouped, G><<<kp.ctas, kThreads, L::total, st>>>(ta, tb, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -1386,6 +1223,317 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp
     }
     gemm_i8_pair_kernel<kGrouped, G><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, tc, kp, kWaitLimitNs);
     return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------
+// Decode GEMM with smoothquant fused in front (swapped operands: the weights
+// are the 128-row MMA operand, at most 16 tokens the MMA N).  One kernel
+// replaces the smoothquant kernel + GEMM pair (rocwmma_smoothquant.cpp:58-122
+// feeding rocwmma_gemm_quantized.cpp:127-195): eight quantising warps read
+// the fp16 tokens, find each token's absmax, and write the whole int8 token
+// operand once into shared memory (16 x K bytes, K <= 8192), in the
+// 128-byte-swizzled K-major layout a TMA load would produce, where it stays
+// for every weight tile the CTA computes.  The weight tiles stream through a
+// ring of 32 KiB stages as in gemm_i8_kernel.  The MMA warp waits, in the
+// CTA's first tile only, for each 2048-wide K chunk of the token operand to
+// be written (one mbarrier per chunk), so the quantisation overlaps the
+// first weight stages.  Every role waits for the previous kernel of the
+// stream (griddepcontrol.wait) before it touches global memory: the kernel
+// is launched with programmatic dependent launch, so only its set-up
+// overlaps the previous kernel.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kSqBN = 16;             // token columns (MMA N)
+constexpr uint32_t kSqBK = 256;            // weight stage depth along K
+constexpr uint32_t kSqST = 3;              // weight stages
+constexpr uint32_t kSqQuantWarps = 8;
+constexpr uint32_t kSqQuantThreads = 32 * kSqQuantWarps;
+constexpr uint32_t kSqThreads = kThreads + kSqQuantThreads;  // 448
+constexpr uint32_t kSqChunkK = 2048;      // token-operand readiness granularity
+constexpr uint32_t kSqMaxChunks = 8;
+constexpr uint32_t kSqAStage = kTileM * kSqBK;                // 32 KiB
+constexpr uint32_t kSqBOff = kSqST * kSqAStage;               // resident token operand
+constexpr uint32_t kSqBarBytes = 512;
+// Resident token operand: 16 rows x (K rounded up to a stage) bytes.
+__host__ __device__ constexpr uint32_t sq_b_bytes(uint32_t K) { return (K + kSqBK - 1) / kSqBK * kSqBK * kSqBN; }
+__host__ __device__ constexpr uint32_t sq_smem_bytes(uint32_t K) { return kSqBOff + sq_b_bytes(K) + kSqBarBytes + 1024; }
+static_assert(sq_smem_bytes(kFusedSqMaxK) <= kSmemBudget, "fused decode shared memory");
+static_assert(kFusedSqMaxRows == kSqBN, "fused decode token tile");
+static_assert(kFusedSqMaxK <= kSqChunkK * kSqMaxChunks, "fused decode chunk barriers");
+
+__global__ void __launch_bounds__(kSqThreads, 1)
+    gemm_i8_decode_sq_kernel(const __grid_constant__ CUtensorMap tmA, const KParams p, uint64_t wait_limit_ns)
+{
+    constexpr uint32_t BN = kSqBN, BK = kSqBK, ST = kSqST;
+    constexpr uint32_t TMEM_COLS = tmem_cols(BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bres = sbase + kSqBOff;  // resident token operand
+    const uint32_t boff = kSqBOff + sq_b_bytes(p.K);
+    const uint32_t full_bar = sbase + boff;
+    const uint32_t empty_bar = full_bar + 8 * ST;
+    const uint32_t tfull_bar = empty_bar + 8 * ST;
+    const uint32_t tempty_bar = tfull_bar + 16;
+    const uint32_t bready_bar = tempty_bar + 16;                // [kSqMaxChunks]
+    const uint32_t scales_bar = bready_bar + 8 * kSqMaxChunks;  // row scales written
+    volatile uint32_t* taddr_slot = reinterpret_cast<volatile uint32_t*>(smem + boff + 8 * ST * 2 + 40 + 8 * kSqMaxChunks);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(taddr_slot + 1);
+    volatile float* s_rs = reinterpret_cast<volatile float*>(taddr_slot + 2);
+    volatile float* s_inv = s_rs + BN;
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t nchunks = (p.K + kSqChunkK - 1) / kSqChunkK;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < ST; ++s) {
+            mbar_init(full_bar + 8 * s, 1);
+            mbar_init(empty_bar + 8 * s, 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar + 8 * b, 1);
+            mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
+        }
+        for (uint32_t c = 0; c < kSqMaxChunks; ++c) mbar_init(bready_bar + 8 * c, kSqQuantWarps);
+        mbar_init(scales_bar, kSqQuantWarps);
+        for (uint32_t r = 0; r < BN; ++r) s_inv[r] = 0.f;  // row maxima accumulate here first
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(const_cast<uint32_t*>(taddr_slot)), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *taddr_slot;
+    const uint32_t T = p.dp_tiles;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ weight producer
+        if (lane == 0) {
+            griddep_wait();
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_phase[ST];
+            bool issued[ST];
+            for (uint32_t s = 0; s < ST; ++s) issued[s] = false, issued_phase[s] = 0;
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < T; t += gridDim.x) {
+                const int32_t a_row = (int32_t)(t * kTileM);
+                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_bar + 8 * stage;
+                    mbar_arrive_expect_tx(fb, kSqAStage);
+                    const uint32_t sa = sbase + stage * kSqAStage;
+#pragma unroll
+                    for (uint32_t i = 0; i < BK / 128; ++i)
+                        tma_load_2d(sa + i * (kTileM * 128), &tmA, fb, (int32_t)(kb * BK + i * 128), a_row);
+                    issued[stage] = true;
+                    issued_phase[stage] = phase;
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+            }
+            for (uint32_t s = 0; s < ST; ++s)
+                if (issued[s]) mbar_wait(full_bar + 8 * s, issued_phase[s], SITE_PRODUCER_DRAIN, nullptr, wait_limit_ns);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_i8(kTileM, BN, 0, 0);
+            uint32_t stage = 0, phase = 0, uidx = 0, ready_chunks = 0;
+            bool ok = true;
+            for (uint32_t t = blockIdx.x; ok && t < T; t += gridDim.x, ++uidx) {
+                const uint32_t buf = uidx & 1, use = uidx >> 1;
+                if (!mbar_wait(tempty_bar + 8 * buf, (use & 1) ^ 1, SITE_MMA_TMEM_EMPTY, abort_flag, wait_limit_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * BN;
+                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+                    // the token operand's K chunk is written (first tile only; it stays)
+                    while (ok && ready_chunks < nchunks && kb * BK >= ready_chunks * kSqChunkK) {
+                        ok = mbar_wait(bready_bar + 8 * ready_chunks, 0, SITE_FUSED_QUANT, abort_flag, wait_limit_ns);
+                        ++ready_chunks;
+                    }
+                    if (!ok || !mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = sbase + stage * kSqAStage;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < BK / 32; ++kk) {
+                        const uint32_t kg = kb * BK + kk * 32;  // K offset of this MMA
+                        const uint64_t ad = umma_desc_sw128(sa + (kk / 4) * (kTileM * 128) + (kk % 4) * 32, 16, 1024);
+                        const uint64_t bd = umma_desc_sw128(bres + (kg / 128) * (BN * 128) + (kg % 128), 16, 1024);
+                        mma_i8(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(empty_bar + 8 * stage);
+                    if (++stage == ST) stage = 0, phase ^= 1;
+                }
+                if (!ok) break;
+                mma_commit(tfull_bar + 8 * buf);
+            }
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ------------------------------------------------------------ epilogue
+        griddep_wait();
+        const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
+        const uint32_t row_local = q * 32 + lane;
+        bool ok = mbar_wait(scales_bar, 0, SITE_FUSED_SCALES, abort_flag, wait_limit_ns);
+        // column scale of column (lane % 16): the token row scale computed in this kernel
+        const float csv = (lane % BN) < p.Nk ? s_rs[lane % BN] : 0.f;
+        uint32_t uidx = 0;
+        for (uint32_t t = blockIdx.x; ok && t < T; t += gridDim.x, ++uidx) {
+            const uint32_t buf = uidx & 1, use = uidx >> 1;
+            if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) break;
+            tc_fence_after();
+            const uint32_t row0 = t * kTileM + row_local;
+            const uint32_t row = row0 < p.Mk ? row0 : 0xffffffffu;
+            const float rsc = (p.row_scale_vec && row < p.Mk) ? __ldg(p.row_scale_vec + row) : p.row_scale;
+            int32_t acc[BN];
+            tmem_ld_chunk<BN>(tmem_base + ((q * 32) << 16) + buf * BN, acc);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
+            store_chunk<BN, false>(p, row, 0, acc, rsc, csv);
+        }
+    } else {
+        // ------------------------------------------------------------ quantising warps
+        griddep_wait();
+        const uint32_t qt = threadIdx.x - kThreads;  // 0 .. 255
+        const float qmax = p.sq_qmax;
+        const bool integral = qmax == truncf(qmax);
+        const uint32_t nvec = p.K / 8;
+        // Pass 1: each token row's absmax of x * s over all of K (reference
+        // :83-96).  A thread takes one 8-element column vector of every row at
+        // a time, so all its loads for that vector are in flight together.
+        float amax[BN];
+#pragma unroll
+        for (uint32_t r = 0; r < BN; ++r) amax[r] = 0.f;
+        for (uint32_t v = qt; v < nvec; v += kSqQuantThreads) {
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8) + 1);
+            uint4 raw[BN];
+#pragma unroll
+            for (uint32_t r = 0; r < BN; ++r)
+                raw[r] = r < p.Nk ? __ldg(reinterpret_cast<const uint4*>(p.sq_x + (size_t)r * p.sq_ldx) + v)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (uint32_t r = 0; r < BN; ++r) {
+                float xf[8];
+                unpack8(raw[r], xf);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) amax[r] = fmaxf(amax[r], fabsf(__fmul_rn(xf[i], sv[i])));
+            }
+        }
+        // Block-wide max per row: warp shuffles, then an integer atomicMax in
+        // shared memory (amax >= 0 and never NaN, so its bits order like ints).
+#pragma unroll
+        for (uint32_t r = 0; r < BN; ++r) {
+            float m = amax[r];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            if (lane == 0) atomicMax(reinterpret_cast<int*>(const_cast<float*>(s_inv + r)), __float_as_int(m));
+        }
+        named_bar_sync(2, kSqQuantThreads);
+        if (qt < BN) {
+            const float rs = row_scale_of(s_inv[qt], qmax);  // reference :95, :98
+            s_rs[qt] = rs;
+            s_inv[qt] = inv_scale_of(rs);
+            if (blockIdx.x == 0 && p.sq_rs_out != nullptr && qt < p.Nk) p.sq_rs_out[qt] = rs;
+        }
+        named_bar_sync(2, kSqQuantThreads);
+        if (lane == 0) mbar_arrive(scales_bar);
+        // Pass 2: the int8 token operand, chunk by chunk.  A thread writes one
+        // 16-byte piece (16 k) of 8 rows per chunk; within a 128-byte-swizzled
+        // K-major atom, row r sits at r * 128 and its piece c at c ^ (r % 8).
+        const uint32_t pieces = p.K / 16;
+        constexpr uint32_t kPiecesPerChunk = kSqChunkK / 16;  // 128: x 2 row groups = 256 items
+        for (uint32_t ch = 0; ch < nchunks; ++ch) {
+            const uint32_t c = ch * kPiecesPerChunk + (qt >> 1);
+            const uint32_t r0 = (qt & 1) * 8;
+            if (c < pieces) {
+                const uint32_t k0 = c * 16;
+                float4 sc[4];
+#pragma unroll
+                for (uint32_t h = 0; h < 4; ++h) sc[h] = __ldg(reinterpret_cast<const float4*>(p.sq_s + k0) + h);
+                uint4 raw[8][2];
+#pragma unroll
+                for (uint32_t i = 0; i < 8; ++i) {
+                    const bool live = r0 + i < p.Nk;
+                    const uint4* xp = reinterpret_cast<const uint4*>(p.sq_x + (size_t)(r0 + i) * p.sq_ldx + k0);
+                    raw[i][0] = live ? __ldg(xp) : make_uint4(0u, 0u, 0u, 0u);
+                    raw[i][1] = live ? __ldg(xp + 1) : make_uint4(0u, 0u, 0u, 0u);
+                }
+                const float sv[16] = {sc[0].x, sc[0].y, sc[0].z, sc[0].w, sc[1].x, sc[1].y, sc[1].z, sc[1].w,
+                                      sc[2].x, sc[2].y, sc[2].z, sc[2].w, sc[3].x, sc[3].y, sc[3].z, sc[3].w};
+#pragma unroll
+                for (uint32_t i = 0; i < 8; ++i) {
+                    const uint32_t r = r0 + i;
+                    uint32_t w[4] = {0u, 0u, 0u, 0u};
+                    if (r < p.Nk) {
+                        const float inv = s_inv[r];
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h) {
+                            float xf[8];
+                            unpack8(raw[i][h], xf);
+                            uint32_t b[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float xs = __fmul_rn(xf[e], sv[8 * h + e]);
+                                b[e] = integral ? quant_bits(xs, inv, qmax) : (uint32_t)(uint8_t)quant1(xs, inv, qmax);
+                            }
+                            w[2 * h] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+                            w[2 * h + 1] = pack_low_bytes(b[4], b[5], b[6], b[7]);
+                        }
+                        if (blockIdx.x == 0 && p.sq_xq_out != nullptr)
+                            *reinterpret_cast<uint4*>(p.sq_xq_out + (size_t)r * p.K + k0) =
+                                make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    sts128(bres + (c / 8) * (BN * 128) + r * 128 + (((c % 8) ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+                }
+            }
+            fence_async_smem();  // the tensor core reads the operand through the async proxy
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bready_bar + 8 * ch);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+cudaError_t launch_decode_sq(const CUtensorMap& ta, const KParams& kp, cudaStream_t st)
+{
+    static std::atomic<uint64_t> done_mask{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done_mask.load() & bit)) {
+        e = cudaFuncSetAttribute(gemm_i8_decode_sq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 sq_smem_bytes(kFusedSqMaxK));
+        if (e != cudaSuccess) return e;
+        done_mask.fetch_or(bit);
+    }
+    return launch_pdl(gemm_i8_decode_sq_kernel, dim3(kp.ctas), dim3(kSqThreads), sq_smem_bytes(kp.K), st, ta, kp,
+                      (uint64_t)kWaitLimitNs);
 }
 
 }  // namespace
@@ -1502,21 +1650,27 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
     if (p.sq_x != nullptr) {
-        // smoothquant fused into the decode GEMM (16-wide token tiles, whole tiles only)
-        if (bn != 16 || s.cta_pair || s.sk_iters != 0 || s.tile_k != tile_k_for(16) || !p.transpose_out ||
-            p.b_mn_major || p.n_extra || p.mc_c) {
-            if (detail) *detail = "internal: fused smoothquant needs the swapped 16-wide decode schedule";
+        // smoothquant fused into the decode GEMM: whole 128-row weight tiles, 16 tokens
+        if (p.Nk > kFusedSqMaxRows || p.K > kFusedSqMaxK || p.K % 16 || !p.transpose_out || p.a_mn_major ||
+            p.b_mn_major || p.n_extra || p.mc_c || s.cta_pair) {
+            if (detail) *detail = "internal: the fused decode kernel needs <= 16 tokens, K <= 8192, K-major weights";
             return cudaErrorInvalidValue;
         }
+        kp.k_blocks = (p.K + kSqBK - 1) / kSqBK;
+        kp.tiles_m = (p.Mk + kTileM - 1) / kTileM;
+        kp.tiles_n = 1;
+        kp.dp_tiles = kp.tiles_m;
+        kp.sk_iters = 0;
+        kp.ctas = s.ctas < kp.dp_tiles ? s.ctas : kp.dp_tiles;
+        kp.col_scale_vec = nullptr;
+        kp.pdl_dep = 0;
         kp.sq_x = static_cast<const uint16_t*>(p.sq_x);
         kp.sq_ldx = p.sq_ldx;
         kp.sq_s = p.sq_s;
         kp.sq_qmax = p.sq_qmax;
         kp.sq_xq_out = p.sq_xq;
         kp.sq_rs_out = p.sq_rs;
-        kp.col_scale_vec = nullptr;
-        kp.pdl_dep = 0;
-        return launch_tile<16, tile_k_for(16), false, false, true>(ta, tb, kp, st);
+        return launch_decode_sq(ta, kp, st);
     }
     // The all-gather epilogue (extra destinations / multicast) is a separate
     // build of each kernel, so plain GEMMs carry none of its code.

@@ -57,8 +57,10 @@ struct GemmProblem {
     float* sq_rs;
 };
 
-// Largest token count the fused smoothquant + decode GEMM takes (its B tile width).
+// Largest token count and K the fused smoothquant + decode GEMM takes (its
+// token tile width; the int8 token operand stays in shared memory whole).
 constexpr uint32_t kFusedSqMaxRows = 16;
+constexpr uint32_t kFusedSqMaxK = 8192;
 
 struct GemmSchedule {
     uint32_t swap_ab;
