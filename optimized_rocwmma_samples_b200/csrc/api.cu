@@ -494,7 +494,7 @@ b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* smooth_scal
     if (!aligned(xq, 16)) return fail(B2SQ_ERR_UNSUPPORTED, "smoothquant_gemm_i8: xq must be 16-byte aligned");
     // Decode sizes with K-major weights: one kernel that quantises the tokens
     // into its own shared-memory B tiles (and writes xq / row_scale once).
-    if (m <= b2sq::kFusedSqMaxRows && k <= b2sq::kFusedSqMaxK && lw == B2SQ_COL_MAJOR &&
+    if (m <= b2sq::kFusedSqMaxRows && n <= b2sq::kFusedSqMaxN && lw == B2SQ_COL_MAJOR &&
         want_swap(m, n, B2SQ_ROW_MAJOR) && k > 0 &&
         aligned(x_f16, 16) && aligned(smooth_scale, 16) && aligned(row_scale, 4) && qmax_ok(quant_max)) {
         if (!x_f16 || !smooth_scale || !row_scale || !xq) return fail(B2SQ_ERR_INVALID_ARG, "smoothquant_gemm_i8: null pointer");

@@ -1230,54 +1230,54 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp
 // Decode GEMM with smoothquant fused in front (swapped operands: the weights
 // are the 128-row MMA operand, at most 16 tokens the MMA N).  One kernel
 // replaces the smoothquant kernel + GEMM pair (rocwmma_smoothquant.cpp:58-122
-// feeding rocwmma_gemm_quantized.cpp:127-195): eight quantising warps read
-// the fp16 tokens, find each token's absmax, and write the whole int8 token
-// operand once into shared memory (16 x K bytes, K <= 8192), in the
-// 128-byte-swizzled K-major layout a TMA load would produce, where it stays
-// for every weight tile the CTA computes.  The weight tiles stream through a
-// ring of 32 KiB stages as in gemm_i8_kernel.  The MMA warp waits, in the
-// CTA's first tile only, for each 2048-wide K chunk of the token operand to
-// be written (one mbarrier per chunk), so the quantisation overlaps the
-// first weight stages.  Every role waits for the previous kernel of the
-// stream (griddepcontrol.wait) before it touches global memory: the kernel
-// is launched with programmatic dependent launch, so only its set-up
-// overlaps the previous kernel.
+// feeding rocwmma_gemm_quantized.cpp:127-195).
+//   * Eight quantising warps read the fp16 tokens, find each token's absmax
+//     (all of K), then write the int8 token operand in 2048-wide K chunks into
+//     two shared-memory chunk buffers, in the 128-byte-swizzled K-major layout
+//     a TMA load would produce.  Each chunk is quantised once per CTA.
+//   * The CTA's weight tiles are walked K-chunk-outer: for each token chunk,
+//     every tile the CTA owns runs that chunk's MMAs into its own TMEM
+//     accumulator, so one resident token chunk serves all of them.  Weight
+//     tiles stream through a ring of 32 KiB stages (160 KiB in flight).
+//   * A chunk buffer is released by an MMA commit once its last MMA is done;
+//     the epilogue runs when every chunk has been accumulated.
+// Every role waits for the previous kernel of the stream (griddepcontrol.wait)
+// before it touches global memory: the kernel is launched with programmatic
+// dependent launch, so only its set-up overlaps the previous kernel.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kSqBN = 16;             // token columns (MMA N)
 constexpr uint32_t kSqBK = 256;            // weight stage depth along K
-constexpr uint32_t kSqST = 3;              // weight stages
+constexpr uint32_t kSqST = 5;              // weight stages
 constexpr uint32_t kSqQuantWarps = 8;
 constexpr uint32_t kSqQuantThreads = 32 * kSqQuantWarps;
 constexpr uint32_t kSqThreads = kThreads + kSqQuantThreads;  // 448
-constexpr uint32_t kSqChunkK = 2048;      // token-operand readiness granularity
-constexpr uint32_t kSqMaxChunks = 8;
+constexpr uint32_t kSqChunkK = 2048;                          // token chunk (K)
+constexpr uint32_t kSqChunkBytes = kSqBN * kSqChunkK;         // 32 KiB
+constexpr uint32_t kSqKbPerChunk = kSqChunkK / kSqBK;
 constexpr uint32_t kSqAStage = kTileM * kSqBK;                // 32 KiB
-constexpr uint32_t kSqBOff = kSqST * kSqAStage;               // resident token operand
+constexpr uint32_t kSqBOff = kSqST * kSqAStage;               // two token chunk buffers
+constexpr uint32_t kSqBarOff = kSqBOff + 2 * kSqChunkBytes;
 constexpr uint32_t kSqBarBytes = 512;
-// Resident token operand: 16 rows x (K rounded up to a stage) bytes.
-__host__ __device__ constexpr uint32_t sq_b_bytes(uint32_t K) { return (K + kSqBK - 1) / kSqBK * kSqBK * kSqBN; }
-__host__ __device__ constexpr uint32_t sq_smem_bytes(uint32_t K) { return kSqBOff + sq_b_bytes(K) + kSqBarBytes + 1024; }
-static_assert(sq_smem_bytes(kFusedSqMaxK) <= kSmemBudget, "fused decode shared memory");
+constexpr uint32_t kSqSmem = kSqBarOff + kSqBarBytes + 1024;
+constexpr uint32_t kSqMaxTilesPerCta = 32;                    // 16 TMEM columns each
+static_assert(kSqSmem <= kSmemBudget, "fused decode shared memory");
 static_assert(kFusedSqMaxRows == kSqBN, "fused decode token tile");
-static_assert(kFusedSqMaxK <= kSqChunkK * kSqMaxChunks, "fused decode chunk barriers");
 
 __global__ void __launch_bounds__(kSqThreads, 1)
     gemm_i8_decode_sq_kernel(const __grid_constant__ CUtensorMap tmA, const KParams p, uint64_t wait_limit_ns)
 {
     constexpr uint32_t BN = kSqBN, BK = kSqBK, ST = kSqST;
-    constexpr uint32_t TMEM_COLS = tmem_cols(BN);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bres = sbase + kSqBOff;  // resident token operand
-    const uint32_t boff = kSqBOff + sq_b_bytes(p.K);
-    const uint32_t full_bar = sbase + boff;
+    const uint32_t bres = sbase + kSqBOff;  // token chunk buffers [2][16 rows x 2048]
+    const uint32_t full_bar = sbase + kSqBarOff;
     const uint32_t empty_bar = full_bar + 8 * ST;
-    const uint32_t tfull_bar = empty_bar + 8 * ST;
-    const uint32_t tempty_bar = tfull_bar + 16;
-    const uint32_t bready_bar = tempty_bar + 16;                // [kSqMaxChunks]
-    const uint32_t scales_bar = bready_bar + 8 * kSqMaxChunks;  // row scales written
-    volatile uint32_t* taddr_slot = reinterpret_cast<volatile uint32_t*>(smem + boff + 8 * ST * 2 + 40 + 8 * kSqMaxChunks);
+    const uint32_t bfull_bar = empty_bar + 8 * ST;  // [2] token chunk written
+    const uint32_t bempty_bar = bfull_bar + 16;     // [2] token chunk no longer read
+    const uint32_t tfull_bar = bempty_bar + 16;     // every accumulator complete
+    const uint32_t scales_bar = tfull_bar + 8;      // row scales written
+    volatile uint32_t* taddr_slot = reinterpret_cast<volatile uint32_t*>(smem + kSqBarOff + 16 * ST + 48);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(taddr_slot + 1);
     volatile float* s_rs = reinterpret_cast<volatile float*>(taddr_slot + 2);
     volatile float* s_inv = s_rs + BN;
@@ -1285,6 +1285,10 @@ __global__ void __launch_bounds__(kSqThreads, 1)
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t nchunks = (p.K + kSqChunkK - 1) / kSqChunkK;
+    const uint32_t T = p.dp_tiles;
+    const uint32_t my_tiles = blockIdx.x < T ? (T - blockIdx.x + gridDim.x - 1) / gridDim.x : 0u;
+    uint32_t tmem_ncols = 32;
+    while (tmem_ncols < my_tiles * BN) tmem_ncols <<= 1;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < ST; ++s) {
@@ -1292,10 +1296,10 @@ __global__ void __launch_bounds__(kSqThreads, 1)
             mbar_init(empty_bar + 8 * s, 1);
         }
         for (uint32_t b = 0; b < 2; ++b) {
-            mbar_init(tfull_bar + 8 * b, 1);
-            mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
+            mbar_init(bfull_bar + 8 * b, kSqQuantWarps);
+            mbar_init(bempty_bar + 8 * b, 1);
         }
-        for (uint32_t c = 0; c < kSqMaxChunks; ++c) mbar_init(bready_bar + 8 * c, kSqQuantWarps);
+        mbar_init(tfull_bar, 1);
         mbar_init(scales_bar, kSqQuantWarps);
         for (uint32_t r = 0; r < BN; ++r) s_inv[r] = 0.f;  // row maxima accumulate here first
         *abort_flag = 0;
@@ -1303,14 +1307,13 @@ __global__ void __launch_bounds__(kSqThreads, 1)
         tma_prefetch_desc(&tmA);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(const_cast<uint32_t*>(taddr_slot)), TMEM_COLS);
+        tmem_alloc(smem_u32(const_cast<uint32_t*>(taddr_slot)), tmem_ncols);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *taddr_slot;
-    const uint32_t T = p.dp_tiles;
 
     if (warp == 0) {
         // ------------------------------------------------------------ weight producer
@@ -1321,22 +1324,25 @@ __global__ void __launch_bounds__(kSqThreads, 1)
             bool issued[ST];
             for (uint32_t s = 0; s < ST; ++s) issued[s] = false, issued_phase[s] = 0;
             bool ok = true;
-            for (uint32_t t = blockIdx.x; ok && t < T; t += gridDim.x) {
-                const int32_t a_row = (int32_t)(t * kTileM);
-                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
-                    if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t fb = full_bar + 8 * stage;
-                    mbar_arrive_expect_tx(fb, kSqAStage);
-                    const uint32_t sa = sbase + stage * kSqAStage;
+            for (uint32_t ch = 0; ok && ch < nchunks; ++ch) {
+                const uint32_t kb1 = (ch + 1) * kSqKbPerChunk < p.k_blocks ? (ch + 1) * kSqKbPerChunk : p.k_blocks;
+                for (uint32_t i = 0; ok && i < my_tiles; ++i) {
+                    const int32_t a_row = (int32_t)((blockIdx.x + i * gridDim.x) * kTileM);
+                    for (uint32_t kb = ch * kSqKbPerChunk; kb < kb1; ++kb) {
+                        if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = full_bar + 8 * stage;
+                        mbar_arrive_expect_tx(fb, kSqAStage);
+                        const uint32_t sa = sbase + stage * kSqAStage;
 #pragma unroll
-                    for (uint32_t i = 0; i < BK / 128; ++i)
-                        tma_load_2d(sa + i * (kTileM * 128), &tmA, fb, (int32_t)(kb * BK + i * 128), a_row);
-                    issued[stage] = true;
-                    issued_phase[stage] = phase;
-                    if (++stage == ST) stage = 0, phase ^= 1;
+                        for (uint32_t a = 0; a < BK / 128; ++a)
+                            tma_load_2d(sa + a * (kTileM * 128), &tmA, fb, (int32_t)(kb * BK + a * 128), a_row);
+                        issued[stage] = true;
+                        issued_phase[stage] = phase;
+                        if (++stage == ST) stage = 0, phase ^= 1;
+                    }
                 }
             }
             for (uint32_t s = 0; s < ST; ++s)
@@ -1347,41 +1353,41 @@ __global__ void __launch_bounds__(kSqThreads, 1)
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_i8(kTileM, BN, 0, 0);
-            uint32_t stage = 0, phase = 0, uidx = 0, ready_chunks = 0;
+            uint32_t stage = 0, phase = 0;
             bool ok = true;
-            for (uint32_t t = blockIdx.x; ok && t < T; t += gridDim.x, ++uidx) {
-                const uint32_t buf = uidx & 1, use = uidx >> 1;
-                if (!mbar_wait(tempty_bar + 8 * buf, (use & 1) ^ 1, SITE_MMA_TMEM_EMPTY, abort_flag, wait_limit_ns)) {
+            for (uint32_t ch = 0; ok && ch < nchunks; ++ch) {
+                const uint32_t buf = ch & 1;
+                if (!mbar_wait(bfull_bar + 8 * buf, (ch >> 1) & 1, SITE_FUSED_QUANT, abort_flag, wait_limit_ns)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + buf * BN;
-                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
-                    // the token operand's K chunk is written (first tile only; it stays)
-                    while (ok && ready_chunks < nchunks && kb * BK >= ready_chunks * kSqChunkK) {
-                        ok = mbar_wait(bready_bar + 8 * ready_chunks, 0, SITE_FUSED_QUANT, abort_flag, wait_limit_ns);
-                        ++ready_chunks;
-                    }
-                    if (!ok || !mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t sa = sbase + stage * kSqAStage;
+                const uint32_t kb0 = ch * kSqKbPerChunk;
+                const uint32_t kb1 = kb0 + kSqKbPerChunk < p.k_blocks ? kb0 + kSqKbPerChunk : p.k_blocks;
+                for (uint32_t i = 0; ok && i < my_tiles; ++i) {
+                    const uint32_t d_tmem = tmem_base + i * BN;
+                    for (uint32_t kb = kb0; kb < kb1; ++kb) {
+                        if (!mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = sbase + stage * kSqAStage;
 #pragma unroll
-                    for (uint32_t kk = 0; kk < BK / 32; ++kk) {
-                        const uint32_t kg = kb * BK + kk * 32;  // K offset of this MMA
-                        const uint64_t ad = umma_desc_sw128(sa + (kk / 4) * (kTileM * 128) + (kk % 4) * 32, 16, 1024);
-                        const uint64_t bd = umma_desc_sw128(bres + (kg / 128) * (BN * 128) + (kg % 128), 16, 1024);
-                        mma_i8(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        for (uint32_t kk = 0; kk < BK / 32; ++kk) {
+                            const uint32_t kl = (kb - kb0) * BK + kk * 32;  // K offset inside the token chunk
+                            const uint64_t ad = umma_desc_sw128(sa + (kk / 4) * (kTileM * 128) + (kk % 4) * 32, 16, 1024);
+                            const uint64_t bd =
+                                umma_desc_sw128(bres + buf * kSqChunkBytes + (kl / 128) * (BN * 128) + (kl % 128), 16, 1024);
+                            mma_i8(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        mma_commit(empty_bar + 8 * stage);
+                        if (++stage == ST) stage = 0, phase ^= 1;
                     }
-                    mma_commit(empty_bar + 8 * stage);
-                    if (++stage == ST) stage = 0, phase ^= 1;
                 }
                 if (!ok) break;
-                mma_commit(tfull_bar + 8 * buf);
+                mma_commit(bempty_bar + 8 * buf);  // this token chunk is no longer read
             }
+            if (ok) mma_commit(tfull_bar);
         }
         __syncwarp();
     } else if (warp < 6) {
@@ -1391,21 +1397,16 @@ __global__ void __launch_bounds__(kSqThreads, 1)
         const uint32_t row_local = q * 32 + lane;
         bool ok = mbar_wait(scales_bar, 0, SITE_FUSED_SCALES, abort_flag, wait_limit_ns);
         // column scale of column (lane % 16): the token row scale computed in this kernel
-        const float csv = (lane % BN) < p.Nk ? s_rs[lane % BN] : 0.f;
-        uint32_t uidx = 0;
-        for (uint32_t t = blockIdx.x; ok && t < T; t += gridDim.x, ++uidx) {
-            const uint32_t buf = uidx & 1, use = uidx >> 1;
-            if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) break;
-            tc_fence_after();
-            const uint32_t row0 = t * kTileM + row_local;
+        const float csv = ok && (lane % BN) < p.Nk ? s_rs[lane % BN] : 0.f;
+        if (ok && my_tiles > 0) ok = mbar_wait(tfull_bar, 0, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns);
+        if (ok) tc_fence_after();
+        for (uint32_t i = 0; ok && i < my_tiles; ++i) {
+            const uint32_t row0 = (blockIdx.x + i * gridDim.x) * kTileM + row_local;
             const uint32_t row = row0 < p.Mk ? row0 : 0xffffffffu;
             const float rsc = (p.row_scale_vec && row < p.Mk) ? __ldg(p.row_scale_vec + row) : p.row_scale;
             int32_t acc[BN];
-            tmem_ld_chunk<BN>(tmem_base + ((q * 32) << 16) + buf * BN, acc);
+            tmem_ld_chunk<BN>(tmem_base + ((q * 32) << 16) + i * BN, acc);
             tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar + 8 * buf);
             store_chunk<BN, false>(p, row, 0, acc, rsc, csv);
         }
     } else {
@@ -1460,9 +1461,16 @@ __global__ void __launch_bounds__(kSqThreads, 1)
         // 16-byte piece (16 k) of 8 rows per chunk; within a 128-byte-swizzled
         // K-major atom, row r sits at r * 128 and its piece c at c ^ (r % 8).
         const uint32_t pieces = p.K / 16;
-        constexpr uint32_t kPiecesPerChunk = kSqChunkK / 16;  // 128: x 2 row groups = 256 items
-        for (uint32_t ch = 0; ch < nchunks; ++ch) {
-            const uint32_t c = ch * kPiecesPerChunk + (qt >> 1);
+        constexpr uint32_t kPiecesPerChunk = kSqChunkK / 16;  // 128, x 2 row groups = 256 items
+        bool ok = true;
+        for (uint32_t ch = 0; ok && ch < nchunks; ++ch) {
+            const uint32_t buf = ch & 1;
+            if (!mbar_wait(bempty_bar + 8 * buf, ((ch >> 1) & 1) ^ 1, SITE_FUSED_QUANT, abort_flag, wait_limit_ns)) {
+                ok = false;
+                break;
+            }
+            const uint32_t cl = qt >> 1;  // piece inside the chunk
+            const uint32_t c = ch * kPiecesPerChunk + cl;
             const uint32_t r0 = (qt & 1) * 8;
             if (c < pieces) {
                 const uint32_t k0 = c * 16;
@@ -1479,6 +1487,7 @@ __global__ void __launch_bounds__(kSqThreads, 1)
                 }
                 const float sv[16] = {sc[0].x, sc[0].y, sc[0].z, sc[0].w, sc[1].x, sc[1].y, sc[1].z, sc[1].w,
                                       sc[2].x, sc[2].y, sc[2].z, sc[2].w, sc[3].x, sc[3].y, sc[3].z, sc[3].w};
+                const uint32_t cbuf = bres + buf * kSqChunkBytes;
 #pragma unroll
                 for (uint32_t i = 0; i < 8; ++i) {
                     const uint32_t r = r0 + i;
@@ -1502,20 +1511,21 @@ __global__ void __launch_bounds__(kSqThreads, 1)
                             *reinterpret_cast<uint4*>(p.sq_xq_out + (size_t)r * p.K + k0) =
                                 make_uint4(w[0], w[1], w[2], w[3]);
                     }
-                    sts128(bres + (c / 8) * (BN * 128) + r * 128 + (((c % 8) ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+                    sts128(cbuf + (cl / 8) * (BN * 128) + r * 128 + (((cl % 8) ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
                 }
             }
             fence_async_smem();  // the tensor core reads the operand through the async proxy
             __syncwarp();
-            if (lane == 0) mbar_arrive(bready_bar + 8 * ch);
+            if (lane == 0) mbar_arrive(bfull_bar + 8 * buf);
         }
+        __syncwarp();
     }
 
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        tmem_dealloc(tmem_base, tmem_ncols);
     }
 }
 
@@ -1527,12 +1537,11 @@ cudaError_t launch_decode_sq(const CUtensorMap& ta, const KParams& kp, cudaStrea
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_decode_sq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 sq_smem_bytes(kFusedSqMaxK));
+        e = cudaFuncSetAttribute(gemm_i8_decode_sq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSqSmem);
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    return launch_pdl(gemm_i8_decode_sq_kernel, dim3(kp.ctas), dim3(kSqThreads), sq_smem_bytes(kp.K), st, ta, kp,
+    return launch_pdl(gemm_i8_decode_sq_kernel, dim3(kp.ctas), dim3(kSqThreads), kSqSmem, st, ta, kp,
                       (uint64_t)kWaitLimitNs);
 }
 
@@ -1651,7 +1660,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     if (kp.ctas == 0) return cudaSuccess;
     if (p.sq_x != nullptr) {
         // smoothquant fused into the decode GEMM: whole 128-row weight tiles, 16 tokens
-        if (p.Nk > kFusedSqMaxRows || p.K > kFusedSqMaxK || p.K % 16 || !p.transpose_out || p.a_mn_major ||
+        if (p.Nk > kFusedSqMaxRows || p.K % 16 || !p.transpose_out || p.a_mn_major ||
             p.b_mn_major || p.n_extra || p.mc_c || s.cta_pair) {
             if (detail) *detail = "internal: the fused decode kernel needs <= 16 tokens, K <= 8192, K-major weights";
             return cudaErrorInvalidValue;
@@ -1662,6 +1671,10 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
         kp.dp_tiles = kp.tiles_m;
         kp.sk_iters = 0;
         kp.ctas = s.ctas < kp.dp_tiles ? s.ctas : kp.dp_tiles;
+        if ((kp.dp_tiles + kp.ctas - 1) / kp.ctas > kSqMaxTilesPerCta) {
+            if (detail) *detail = "internal: too many weight tiles per CTA for the fused decode kernel";
+            return cudaErrorInvalidValue;
+        }
         kp.col_scale_vec = nullptr;
         kp.pdl_dep = 0;
         kp.sq_x = static_cast<const uint16_t*>(p.sq_x);

@@ -57,10 +57,10 @@ struct GemmProblem {
     float* sq_rs;
 };
 
-// Largest token count and K the fused smoothquant + decode GEMM takes (its
-// token tile width; the int8 token operand stays in shared memory whole).
+// Largest token count the fused smoothquant + decode GEMM takes (its token
+// tile width), and the most weight rows (148 CTAs x 32 tiles of 128 rows).
 constexpr uint32_t kFusedSqMaxRows = 16;
-constexpr uint32_t kFusedSqMaxK = 8192;
+constexpr uint32_t kFusedSqMaxN = 148u * 32u * 128u;
 
 struct GemmSchedule {
     uint32_t swap_ab;
