@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64", "fused16"], default=None,
+    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64"], default=None,
                     help="run 3 launches of one kernel on its workload and exit (for ncu captures)")
     return ap.parse_args()
 
@@ -79,13 +79,6 @@ def run_profile(kind: str):
         s = torch.ones((SQ_K,), device=dev)
         for _ in range(3):
             api.smoothquant(x, s)
-    elif kind == "fused16":  # config 3, M = 16: smoothquant inside the decode GEMM
-        x = torch.randn((16, K), device=dev).to(torch.float16)
-        s = torch.empty((K,), device=dev).uniform_(0.5, 2.0)
-        w = synth.torch_int8_uniform((28672, K), dev, 2)
-        sb = synth.torch_scales(28672, dev, 4)
-        for _ in range(3):
-            api.smoothquant_gemm(x, s, w, sb, out_dtype=torch.float16)
     else:
         m = {"gemm": M, "decode16": 16, "decode64": 64}[kind]
         n = N if kind == "gemm" else 28672
@@ -468,7 +461,7 @@ def n1_sections(args, dev, api, synth, timed, l2_flush, stream, hbm_gbs, ws):
         bytes_d = (md * K * 2 + md * K + K * 4 + md * 4) + (md * K + 28672 * K + 4 * 28672 + 4 * md + 2 * md * 28672)
         decode[f"m{md}"] = {"ms": r4(ms_d), "gbs": r4(bytes_d / (ms_d * 1e-3) / 1e9),
                             "frac_of_measured_hbm": r4(bytes_d / (ms_d * 1e-3) / 1e9 / hbm_gbs),
-                            "shape": [md, K, 28672], "gpu_launches_per_step": 1 if md <= 16 else 2}
+                            "shape": [md, K, 28672], "gpu_launches_per_step": 2}
     out["decode"] = decode
     del w_dec
 

@@ -274,22 +274,11 @@ namespace {
 // Body of b2sq_gemm_i8.  a_from_prev_kernel: the A operand and scale_a_row
 // are written by the kernel enqueued just before on the same stream; the GEMM
 // is then launched with programmatic dependent launch.
-// Smoothquant fused into the decode GEMM: A (the tokens) is computed inside
-// the GEMM from these fp16 activations instead of read.
-struct SqFuse {
-    const void* x;
-    const float* smooth;
-    float qmax;
-    int8_t* xq;
-    float* row_scale;
-};
-
 b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2sq_layout la, uint32_t lda,
                          const int8_t* b, b2sq_layout lb, uint32_t ldb, void* c, b2sq_dtype c_type, uint32_t ldc,
                          const float* scale_a_row, const float* scale_b_col, float scale_a, float scale_b,
                          void* workspace, size_t workspace_bytes, b2sq_stream_t stream, bool a_from_prev_kernel,
-                         void* const* extra_c = nullptr, uint32_t n_extra = 0, void* mc_c = nullptr,
-                         const SqFuse* fuse = nullptr)
+                         void* const* extra_c = nullptr, uint32_t n_extra = 0, void* mc_c = nullptr)
 {
     b2sq_status st = validate_gemm(m, n, k, a, la, lda, b, lb, ldb, c, c_type, ldc, scale_a_row, scale_b_col);
     if (st != B2SQ_OK || m == 0 || n == 0) return st;
@@ -339,15 +328,6 @@ b2sq_status gemm_i8_impl(uint32_t m, uint32_t n, uint32_t k, const int8_t* a, b2
         p.col_scale_vec = scale_b_col;
         p.row_scale = scale_a;
         p.col_scale = scale_b;
-    }
-    if (fuse) {
-        p.sq_x = fuse->x;
-        p.sq_ldx = k;
-        p.sq_s = fuse->smooth;
-        p.sq_qmax = fuse->qmax;
-        p.sq_xq = fuse->xq;
-        p.sq_rs = fuse->row_scale;
-        p.pdl_dep = 0;
     }
     b2sq::GemmSchedule s;
     b2sq::plan_gemm_schedule(p.Mk, p.Nk, k, p.a_mn_major, p.b_mn_major, workspace != nullptr, sms, s);
@@ -492,16 +472,6 @@ b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* smooth_scal
     if (m == 0 || n == 0) return ok();
     if (k % 16) return fail(B2SQ_ERR_UNSUPPORTED, "smoothquant_gemm_i8: k must be a multiple of 16 (TMA)");
     if (!aligned(xq, 16)) return fail(B2SQ_ERR_UNSUPPORTED, "smoothquant_gemm_i8: xq must be 16-byte aligned");
-    // Decode sizes with K-major weights: one kernel that quantises the tokens
-    // into its own shared-memory B tiles (and writes xq / row_scale once).
-    if (m <= b2sq::kFusedSqMaxRows && n <= b2sq::kFusedSqMaxN && lw == B2SQ_COL_MAJOR &&
-        want_swap(m, n, B2SQ_ROW_MAJOR) && k > 0 &&
-        aligned(x_f16, 16) && aligned(smooth_scale, 16) && aligned(row_scale, 4) && qmax_ok(quant_max)) {
-        if (!x_f16 || !smooth_scale || !row_scale || !xq) return fail(B2SQ_ERR_INVALID_ARG, "smoothquant_gemm_i8: null pointer");
-        const SqFuse f{x_f16, smooth_scale, quant_max, xq, row_scale};
-        return gemm_i8_impl(m, n, k, xq, B2SQ_ROW_MAJOR, k, w, lw, ldw, c, c_type, ldc, nullptr, scale_w_col, 1.f,
-                            scale_w, workspace, workspace_bytes, stream, false, nullptr, 0, nullptr, &f);
-    }
     b2sq_status st = b2sq_smoothquant(x_f16, smooth_scale, xq, row_scale, m, k, quant_max, stream);
     if (st != B2SQ_OK) return st;
     return gemm_i8_impl(m, n, k, xq, B2SQ_ROW_MAJOR, k, w, lw, ldw, c, c_type, ldc, row_scale, scale_w_col, 1.f,

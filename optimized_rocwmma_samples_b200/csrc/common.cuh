@@ -38,8 +38,6 @@ enum WaitSite : uint32_t {
     SITE_SQ_PRODUCER = 11,
     SITE_SQ_CONSUMER = 12,
     SITE_SQ_DRAIN = 13,
-    SITE_FUSED_QUANT = 14,   // decode GEMM's quantising warps waiting for a free stage
-    SITE_FUSED_SCALES = 15,  // decode GEMM's epilogue waiting for the row scales
     SITE_DEBUG = 100,
 };
 

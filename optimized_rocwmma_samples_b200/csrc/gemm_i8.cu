@@ -32,7 +32,6 @@
 //  * no TMA multicast anywhere (every CTA loads its own tiles).
 #include "common.cuh"
 #include "kernels.h"
-#include "sq_math.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -102,17 +101,6 @@ struct KParams {
     // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
     // row scales) are written by the kernel launched just before this one.
     uint32_t pdl_dep;
-    // Decode GEMM with smoothquant fused in front (gemm_i8_decode_sq_kernel):
-    // the token operand is quantised in the kernel from fp16 sq_x [Nk, K]
-    // (pitch sq_ldx elements) and smooth scales sq_s [K]; CTA 0 also writes
-    // the int8 rows to sq_xq_out [Nk, K] and the row scales to sq_rs_out [Nk]
-    // (each nullable).  The row scales are the kernel's column scales.
-    const uint16_t* sq_x;
-    uint32_t sq_ldx;
-    const float* sq_s;
-    float sq_qmax;
-    int8_t* sq_xq_out;
-    float* sq_rs_out;
 };
 
 constexpr uint32_t kTileK_Grouped = tile_k_for(256);
@@ -1225,326 +1213,6 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp
     return cudaGetLastError();
 }
 
-
-// ---------------------------------------------------------------------------
-// Decode GEMM with smoothquant fused in front (swapped operands: the weights
-// are the 128-row MMA operand, at most 16 tokens the MMA N).  One kernel
-// replaces the smoothquant kernel + GEMM pair (rocwmma_smoothquant.cpp:58-122
-// feeding rocwmma_gemm_quantized.cpp:127-195).
-//   * Eight quantising warps read the fp16 tokens, find each token's absmax
-//     (all of K), then write the int8 token operand in 2048-wide K chunks into
-//     two shared-memory chunk buffers, in the 128-byte-swizzled K-major layout
-//     a TMA load would produce.  Each chunk is quantised once per CTA.
-//   * The CTA's weight tiles are walked K-chunk-outer: for each token chunk,
-//     every tile the CTA owns runs that chunk's MMAs into its own TMEM
-//     accumulator, so one resident token chunk serves all of them.  Weight
-//     tiles stream through a ring of 32 KiB stages (160 KiB in flight).
-//   * A chunk buffer is released by an MMA commit once its last MMA is done;
-//     the epilogue runs when every chunk has been accumulated.
-// Every role waits for the previous kernel of the stream (griddepcontrol.wait)
-// before it touches global memory: the kernel is launched with programmatic
-// dependent launch, so only its set-up overlaps the previous kernel.
-// ---------------------------------------------------------------------------
-constexpr uint32_t kSqBN = 16;             // token columns (MMA N)
-constexpr uint32_t kSqBK = 256;            // weight stage depth along K
-constexpr uint32_t kSqST = 5;              // weight stages
-constexpr uint32_t kSqQuantWarps = 8;
-constexpr uint32_t kSqQuantThreads = 32 * kSqQuantWarps;
-constexpr uint32_t kSqThreads = kThreads + kSqQuantThreads;  // 448
-constexpr uint32_t kSqChunkK = 2048;                          // token chunk (K)
-constexpr uint32_t kSqChunkBytes = kSqBN * kSqChunkK;         // 32 KiB
-constexpr uint32_t kSqKbPerChunk = kSqChunkK / kSqBK;
-constexpr uint32_t kSqAStage = kTileM * kSqBK;                // 32 KiB
-constexpr uint32_t kSqBOff = kSqST * kSqAStage;               // two token chunk buffers
-constexpr uint32_t kSqBarOff = kSqBOff + 2 * kSqChunkBytes;
-constexpr uint32_t kSqBarBytes = 512;
-constexpr uint32_t kSqSmem = kSqBarOff + kSqBarBytes + 1024;
-constexpr uint32_t kSqMaxTilesPerCta = 32;                    // 16 TMEM columns each
-static_assert(kSqSmem <= kSmemBudget, "fused decode shared memory");
-static_assert(kFusedSqMaxRows == kSqBN, "fused decode token tile");
-
-__global__ void __launch_bounds__(kSqThreads, 1)
-    gemm_i8_decode_sq_kernel(const __grid_constant__ CUtensorMap tmA, const KParams p, uint64_t wait_limit_ns)
-{
-    constexpr uint32_t BN = kSqBN, BK = kSqBK, ST = kSqST;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t sbase = smem_u32(smem);
-    const uint32_t bres = sbase + kSqBOff;  // token chunk buffers [2][16 rows x 2048]
-    const uint32_t full_bar = sbase + kSqBarOff;
-    const uint32_t empty_bar = full_bar + 8 * ST;
-    const uint32_t bfull_bar = empty_bar + 8 * ST;  // [2] token chunk written
-    const uint32_t bempty_bar = bfull_bar + 16;     // [2] token chunk no longer read
-    const uint32_t tfull_bar = bempty_bar + 16;     // every accumulator complete
-    const uint32_t scales_bar = tfull_bar + 8;      // row scales written
-    volatile uint32_t* taddr_slot = reinterpret_cast<volatile uint32_t*>(smem + kSqBarOff + 16 * ST + 48);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(taddr_slot + 1);
-    volatile float* s_rs = reinterpret_cast<volatile float*>(taddr_slot + 2);
-    volatile float* s_inv = s_rs + BN;
-
-    const uint32_t warp = threadIdx.x >> 5;
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t nchunks = (p.K + kSqChunkK - 1) / kSqChunkK;
-    const uint32_t T = p.dp_tiles;
-    const uint32_t my_tiles = blockIdx.x < T ? (T - blockIdx.x + gridDim.x - 1) / gridDim.x : 0u;
-    uint32_t tmem_ncols = 32;
-    while (tmem_ncols < my_tiles * BN) tmem_ncols <<= 1;
-
-    if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < ST; ++s) {
-            mbar_init(full_bar + 8 * s, 1);
-            mbar_init(empty_bar + 8 * s, 1);
-        }
-        for (uint32_t b = 0; b < 2; ++b) {
-            mbar_init(bfull_bar + 8 * b, kSqQuantWarps);
-            mbar_init(bempty_bar + 8 * b, 1);
-        }
-        mbar_init(tfull_bar, 1);
-        mbar_init(scales_bar, kSqQuantWarps);
-        for (uint32_t r = 0; r < BN; ++r) s_inv[r] = 0.f;  // row maxima accumulate here first
-        *abort_flag = 0;
-        fence_barrier_init();
-        tma_prefetch_desc(&tmA);
-    }
-    if (warp == 1) {
-        tmem_alloc(smem_u32(const_cast<uint32_t*>(taddr_slot)), tmem_ncols);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *taddr_slot;
-
-    if (warp == 0) {
-        // ------------------------------------------------------------ weight producer
-        if (lane == 0) {
-            griddep_wait();
-            uint32_t stage = 0, phase = 0;
-            uint32_t issued_phase[ST];
-            bool issued[ST];
-            for (uint32_t s = 0; s < ST; ++s) issued[s] = false, issued_phase[s] = 0;
-            bool ok = true;
-            for (uint32_t ch = 0; ok && ch < nchunks; ++ch) {
-                const uint32_t kb1 = (ch + 1) * kSqKbPerChunk < p.k_blocks ? (ch + 1) * kSqKbPerChunk : p.k_blocks;
-                for (uint32_t i = 0; ok && i < my_tiles; ++i) {
-                    const int32_t a_row = (int32_t)((blockIdx.x + i * gridDim.x) * kTileM);
-                    for (uint32_t kb = ch * kSqKbPerChunk; kb < kb1; ++kb) {
-                        if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
-                            ok = false;
-                            break;
-                        }
-                        const uint32_t fb = full_bar + 8 * stage;
-                        mbar_arrive_expect_tx(fb, kSqAStage);
-                        const uint32_t sa = sbase + stage * kSqAStage;
-#pragma unroll
-                        for (uint32_t a = 0; a < BK / 128; ++a)
-                            tma_load_2d(sa + a * (kTileM * 128), &tmA, fb, (int32_t)(kb * BK + a * 128), a_row);
-                        issued[stage] = true;
-                        issued_phase[stage] = phase;
-                        if (++stage == ST) stage = 0, phase ^= 1;
-                    }
-                }
-            }
-            for (uint32_t s = 0; s < ST; ++s)
-                if (issued[s]) mbar_wait(full_bar + 8 * s, issued_phase[s], SITE_PRODUCER_DRAIN, nullptr, wait_limit_ns);
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_i8(kTileM, BN, 0, 0);
-            uint32_t stage = 0, phase = 0;
-            bool ok = true;
-            for (uint32_t ch = 0; ok && ch < nchunks; ++ch) {
-                const uint32_t buf = ch & 1;
-                if (!mbar_wait(bfull_bar + 8 * buf, (ch >> 1) & 1, SITE_FUSED_QUANT, abort_flag, wait_limit_ns)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t kb0 = ch * kSqKbPerChunk;
-                const uint32_t kb1 = kb0 + kSqKbPerChunk < p.k_blocks ? kb0 + kSqKbPerChunk : p.k_blocks;
-                for (uint32_t i = 0; ok && i < my_tiles; ++i) {
-                    const uint32_t d_tmem = tmem_base + i * BN;
-                    for (uint32_t kb = kb0; kb < kb1; ++kb) {
-                        if (!mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t sa = sbase + stage * kSqAStage;
-#pragma unroll
-                        for (uint32_t kk = 0; kk < BK / 32; ++kk) {
-                            const uint32_t kl = (kb - kb0) * BK + kk * 32;  // K offset inside the token chunk
-                            const uint64_t ad = umma_desc_sw128(sa + (kk / 4) * (kTileM * 128) + (kk % 4) * 32, 16, 1024);
-                            const uint64_t bd =
-                                umma_desc_sw128(bres + buf * kSqChunkBytes + (kl / 128) * (BN * 128) + (kl % 128), 16, 1024);
-                            mma_i8(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        mma_commit(empty_bar + 8 * stage);
-                        if (++stage == ST) stage = 0, phase ^= 1;
-                    }
-                }
-                if (!ok) break;
-                mma_commit(bempty_bar + 8 * buf);  // this token chunk is no longer read
-            }
-            if (ok) mma_commit(tfull_bar);
-        }
-        __syncwarp();
-    } else if (warp < 6) {
-        // ------------------------------------------------------------ epilogue
-        griddep_wait();
-        const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
-        const uint32_t row_local = q * 32 + lane;
-        bool ok = mbar_wait(scales_bar, 0, SITE_FUSED_SCALES, abort_flag, wait_limit_ns);
-        // column scale of column (lane % 16): the token row scale computed in this kernel
-        const float csv = ok && (lane % BN) < p.Nk ? s_rs[lane % BN] : 0.f;
-        if (ok && my_tiles > 0) ok = mbar_wait(tfull_bar, 0, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns);
-        if (ok) tc_fence_after();
-        for (uint32_t i = 0; ok && i < my_tiles; ++i) {
-            const uint32_t row0 = (blockIdx.x + i * gridDim.x) * kTileM + row_local;
-            const uint32_t row = row0 < p.Mk ? row0 : 0xffffffffu;
-            const float rsc = (p.row_scale_vec && row < p.Mk) ? __ldg(p.row_scale_vec + row) : p.row_scale;
-            int32_t acc[BN];
-            tmem_ld_chunk<BN>(tmem_base + ((q * 32) << 16) + i * BN, acc);
-            tmem_ld_wait();
-            store_chunk<BN, false>(p, row, 0, acc, rsc, csv);
-        }
-    } else {
-        // ------------------------------------------------------------ quantising warps
-        griddep_wait();
-        const uint32_t qt = threadIdx.x - kThreads;  // 0 .. 255
-        const float qmax = p.sq_qmax;
-        const bool integral = qmax == truncf(qmax);
-        const uint32_t nvec = p.K / 8;
-        // Pass 1: each token row's absmax of x * s over all of K (reference
-        // :83-96).  A thread takes one 8-element column vector of every row at
-        // a time, so all its loads for that vector are in flight together.
-        float amax[BN];
-#pragma unroll
-        for (uint32_t r = 0; r < BN; ++r) amax[r] = 0.f;
-        for (uint32_t v = qt; v < nvec; v += kSqQuantThreads) {
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.sq_s + (size_t)v * 8) + 1);
-            uint4 raw[BN];
-#pragma unroll
-            for (uint32_t r = 0; r < BN; ++r)
-                raw[r] = r < p.Nk ? __ldg(reinterpret_cast<const uint4*>(p.sq_x + (size_t)r * p.sq_ldx) + v)
-                                  : make_uint4(0u, 0u, 0u, 0u);
-            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-            for (uint32_t r = 0; r < BN; ++r) {
-                float xf[8];
-                unpack8(raw[r], xf);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) amax[r] = fmaxf(amax[r], fabsf(__fmul_rn(xf[i], sv[i])));
-            }
-        }
-        // Block-wide max per row: warp shuffles, then an integer atomicMax in
-        // shared memory (amax >= 0 and never NaN, so its bits order like ints).
-#pragma unroll
-        for (uint32_t r = 0; r < BN; ++r) {
-            float m = amax[r];
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            if (lane == 0) atomicMax(reinterpret_cast<int*>(const_cast<float*>(s_inv + r)), __float_as_int(m));
-        }
-        named_bar_sync(2, kSqQuantThreads);
-        if (qt < BN) {
-            const float rs = row_scale_of(s_inv[qt], qmax);  // reference :95, :98
-            s_rs[qt] = rs;
-            s_inv[qt] = inv_scale_of(rs);
-            if (blockIdx.x == 0 && p.sq_rs_out != nullptr && qt < p.Nk) p.sq_rs_out[qt] = rs;
-        }
-        named_bar_sync(2, kSqQuantThreads);
-        if (lane == 0) mbar_arrive(scales_bar);
-        // Pass 2: the int8 token operand, chunk by chunk.  A thread writes one
-        // 16-byte piece (16 k) of 8 rows per chunk; within a 128-byte-swizzled
-        // K-major atom, row r sits at r * 128 and its piece c at c ^ (r % 8).
-        const uint32_t pieces = p.K / 16;
-        constexpr uint32_t kPiecesPerChunk = kSqChunkK / 16;  // 128, x 2 row groups = 256 items
-        bool ok = true;
-        for (uint32_t ch = 0; ok && ch < nchunks; ++ch) {
-            const uint32_t buf = ch & 1;
-            if (!mbar_wait(bempty_bar + 8 * buf, ((ch >> 1) & 1) ^ 1, SITE_FUSED_QUANT, abort_flag, wait_limit_ns)) {
-                ok = false;
-                break;
-            }
-            const uint32_t cl = qt >> 1;  // piece inside the chunk
-            const uint32_t c = ch * kPiecesPerChunk + cl;
-            const uint32_t r0 = (qt & 1) * 8;
-            if (c < pieces) {
-                const uint32_t k0 = c * 16;
-                float4 sc[4];
-#pragma unroll
-                for (uint32_t h = 0; h < 4; ++h) sc[h] = __ldg(reinterpret_cast<const float4*>(p.sq_s + k0) + h);
-                uint4 raw[8][2];
-#pragma unroll
-                for (uint32_t i = 0; i < 8; ++i) {
-                    const bool live = r0 + i < p.Nk;
-                    const uint4* xp = reinterpret_cast<const uint4*>(p.sq_x + (size_t)(r0 + i) * p.sq_ldx + k0);
-                    raw[i][0] = live ? __ldg(xp) : make_uint4(0u, 0u, 0u, 0u);
-                    raw[i][1] = live ? __ldg(xp + 1) : make_uint4(0u, 0u, 0u, 0u);
-                }
-                const float sv[16] = {sc[0].x, sc[0].y, sc[0].z, sc[0].w, sc[1].x, sc[1].y, sc[1].z, sc[1].w,
-                                      sc[2].x, sc[2].y, sc[2].z, sc[2].w, sc[3].x, sc[3].y, sc[3].z, sc[3].w};
-                const uint32_t cbuf = bres + buf * kSqChunkBytes;
-#pragma unroll
-                for (uint32_t i = 0; i < 8; ++i) {
-                    const uint32_t r = r0 + i;
-                    uint32_t w[4] = {0u, 0u, 0u, 0u};
-                    if (r < p.Nk) {
-                        const float inv = s_inv[r];
-#pragma unroll
-                        for (uint32_t h = 0; h < 2; ++h) {
-                            float xf[8];
-                            unpack8(raw[i][h], xf);
-                            uint32_t b[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const float xs = __fmul_rn(xf[e], sv[8 * h + e]);
-                                b[e] = integral ? quant_bits(xs, inv, qmax) : (uint32_t)(uint8_t)quant1(xs, inv, qmax);
-                            }
-                            w[2 * h] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-                            w[2 * h + 1] = pack_low_bytes(b[4], b[5], b[6], b[7]);
-                        }
-                        if (blockIdx.x == 0 && p.sq_xq_out != nullptr)
-                            *reinterpret_cast<uint4*>(p.sq_xq_out + (size_t)r * p.K + k0) =
-                                make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                    sts128(cbuf + (cl / 8) * (BN * 128) + r * 128 + (((cl % 8) ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
-                }
-            }
-            fence_async_smem();  // the tensor core reads the operand through the async proxy
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bfull_bar + 8 * buf);
-        }
-        __syncwarp();
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, tmem_ncols);
-    }
-}
-
-cudaError_t launch_decode_sq(const CUtensorMap& ta, const KParams& kp, cudaStream_t st)
-{
-    static std::atomic<uint64_t> done_mask{0};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    const uint64_t bit = 1ull << (dev & 63);
-    if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_decode_sq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSqSmem);
-        if (e != cudaSuccess) return e;
-        done_mask.fetch_or(bit);
-    }
-    return launch_pdl(gemm_i8_decode_sq_kernel, dim3(kp.ctas), dim3(kSqThreads), kSqSmem, st, ta, kp,
-                      (uint64_t)kWaitLimitNs);
-}
-
 }  // namespace
 
 void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_major, uint32_t b_mn_major,
@@ -1658,33 +1326,6 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     kp.raster_group = B2SQ_RASTER_GROUP;
     kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
-    if (p.sq_x != nullptr) {
-        // smoothquant fused into the decode GEMM: whole 128-row weight tiles, 16 tokens
-        if (p.Nk > kFusedSqMaxRows || p.K % 16 || !p.transpose_out || p.a_mn_major ||
-            p.b_mn_major || p.n_extra || p.mc_c || s.cta_pair) {
-            if (detail) *detail = "internal: the fused decode kernel needs <= 16 tokens, K <= 8192, K-major weights";
-            return cudaErrorInvalidValue;
-        }
-        kp.k_blocks = (p.K + kSqBK - 1) / kSqBK;
-        kp.tiles_m = (p.Mk + kTileM - 1) / kTileM;
-        kp.tiles_n = 1;
-        kp.dp_tiles = kp.tiles_m;
-        kp.sk_iters = 0;
-        kp.ctas = s.ctas < kp.dp_tiles ? s.ctas : kp.dp_tiles;
-        if ((kp.dp_tiles + kp.ctas - 1) / kp.ctas > kSqMaxTilesPerCta) {
-            if (detail) *detail = "internal: too many weight tiles per CTA for the fused decode kernel";
-            return cudaErrorInvalidValue;
-        }
-        kp.col_scale_vec = nullptr;
-        kp.pdl_dep = 0;
-        kp.sq_x = static_cast<const uint16_t*>(p.sq_x);
-        kp.sq_ldx = p.sq_ldx;
-        kp.sq_s = p.sq_s;
-        kp.sq_qmax = p.sq_qmax;
-        kp.sq_xq_out = p.sq_xq;
-        kp.sq_rs_out = p.sq_rs;
-        return launch_decode_sq(ta, kp, st);
-    }
     // The all-gather epilogue (extra destinations / multicast) is a separate
     // build of each kernel, so plain GEMMs carry none of its code.
     const bool gather = p.n_extra > 0 || p.mc_c != nullptr;

@@ -44,23 +44,8 @@ struct GemmProblem {
     // this NVSwitch multicast address (mapping every rank's buffer at the
     // offset of c) with multimem.st, instead of to c.
     void* mc_c;
-    // Fused smoothquant (decode, swapped operands): when sq_x is set, the
-    // kernel B operand (the tokens) is quantised inside the GEMM from fp16
-    // sq_x [Nk, K] (pitch sq_ldx elements) with smooth scales sq_s [K] and
-    // quant max sq_qmax; b / col_scale_vec are then unused, and sq_xq /
-    // sq_rs (nullable) receive the int8 rows and the row scales.
-    const void* sq_x;
-    uint32_t sq_ldx;
-    const float* sq_s;
-    float sq_qmax;
-    int8_t* sq_xq;
-    float* sq_rs;
 };
 
-// Largest token count the fused smoothquant + decode GEMM takes (its token
-// tile width), and the most weight rows (148 CTAs x 32 tiles of 128 rows).
-constexpr uint32_t kFusedSqMaxRows = 16;
-constexpr uint32_t kFusedSqMaxN = 148u * 32u * 128u;
 
 struct GemmSchedule {
     uint32_t swap_ab;

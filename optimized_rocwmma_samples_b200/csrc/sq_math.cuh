@@ -1,6 +1,5 @@
-// sq_math.cuh — the per-element arithmetic of smoothquant, shared by the
-// smoothquant kernels and the decode GEMM that quantises its activations
-// itself.  Reference operation order (rocwmma_smoothquant.cpp:83-120), fp32:
+// sq_math.cuh — the per-element arithmetic of smoothquant (dense and MoE
+// kernels).  Reference operation order (rocwmma_smoothquant.cpp:83-120), fp32:
 //   xs = float(x) * s;  rs = amax / qmax;  inv = rs > 0 ? 1 / rs : 0;
 //   q = int8(fminf(fmaxf(rintf(xs * inv), -qmax), qmax))
 #pragma once

@@ -80,12 +80,11 @@ def test_fused_decode_replays_in_a_cuda_graph(cuda_device):
 
 @pytest.mark.parametrize("M,K,N,qmax", [(16, 1040, 4096, 127.0), (3, 8192, 28672, 127.0), (11, 4112, 2304, 100.5),
                                         (16, 2048, 512, 7.0), (1, 16, 256, 127.0)])
-def test_single_kernel_decode_matches_two_calls(cuda_device, M, K, N, qmax):
-    """Decode sizes (M <= 16, K-major weights) run as ONE kernel that
-    quantises the tokens into its own shared-memory operand tiles: Xq, row
-    scales and the fp16 output are bit-identical to b2sq_smoothquant followed
-    by b2sq_gemm_i8, including ragged K, fractional quant_max and rows with
-    inf / NaN / all-zero inputs."""
+def test_decode_edge_cases_match_two_calls(cuda_device, M, K, N, qmax):
+    """Decode sizes through the one-call entry: Xq, row scales and the fp16
+    output are bit-identical to b2sq_smoothquant followed by b2sq_gemm_i8,
+    including ragged K, fractional quant_max and rows with inf / NaN /
+    all-zero inputs."""
     dev = cuda_device
     rng = np.random.default_rng(M * 7 + K)
     xn = synth.activations_np(rng, M, K, 4, 30.0)
