@@ -101,12 +101,6 @@ struct KParams {
     // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
     // row scales) are written by the kernel launched just before this one.
     uint32_t pdl_dep;
-    // CTA-pair narrow tail (gemm_i8_pair_kernel<.., kTail = true>): the tiles
-    // of the last, partly filled round are each cut into tail_split column
-    // slices of 256 / tail_split (pair tile indices from tail_first on), so
-    // the round's slices keep every pair busy for a fraction of a tile time.
-    uint32_t tail_first;
-    uint32_t tail_split;
 };
 
 constexpr uint32_t kTileK_Grouped = tile_k_for(256);
@@ -909,36 +903,11 @@ __device__ __forceinline__ PairTile pair_tile(const KParams& p, uint32_t t, cons
     return g;
 }
 
-// Pair tile t of the narrow-tail schedule: whole 256-column tiles before
-// p.tail_first, then each remaining tile cut into p.tail_split column slices
-// (consecutive t, so a tile's slices go to different pairs).  *width gets the
-// slice's column count.
-__device__ __forceinline__ PairTile pair_tile_tail(const KParams& p, uint32_t t, uint32_t* width)
-{
-    if (t < p.tail_first) {
-        *width = kPairBN;
-        return pair_tile<false>(p, t, nullptr);
-    }
-    const uint32_t j = t - p.tail_first;
-    const uint32_t w = kPairBN / p.tail_split;
-    PairTile g = pair_tile<false>(p, p.tail_first + j / p.tail_split, nullptr);
-    const uint32_t off = (j % p.tail_split) * w;
-    g.b_row += off;
-    g.col0 += off;
-    *width = w;
-    return g;
-}
-
-// kTail: the narrow-tail build (K-major B only, no grouping, no all-gather):
-// tmBn is B's tensor map with a box of 128 / tail_split rows for the slices;
-// the plain build ignores it.
-template <bool kGrouped, bool G = false, bool kTail = false>
+template <bool kGrouped, bool G = false>
 __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmBn,
-                        const KParams p, uint64_t wait_limit_ns)
+                        const __grid_constant__ CUtensorMap tmC, const KParams p, uint64_t wait_limit_ns)
 {
-    static_assert(!kTail || (!kGrouped && !G), "the narrow tail is a plain-GEMM build");
     constexpr uint32_t ST = kPairST;
     constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
     extern __shared__ uint8_t smem_raw[];
@@ -957,7 +926,6 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     const uint32_t pair = blockIdx.x >> 1;
     const uint32_t npairs = gridDim.x >> 1;
     uint32_t T = p.tiles_m * p.tiles_n;
-    if constexpr (kTail) T = p.tail_first + (T - p.tail_first) * p.tail_split;
     const uint32_t* gpre = nullptr;  // grouped mode: pair-tile prefix per group, [groups + 1]
     if constexpr (kGrouped) {
         __shared__ uint32_t s_gpre[kMaxGroups + 1];
@@ -988,7 +956,6 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
-        if constexpr (kTail) tma_prefetch_desc(&tmBn);
         if (!G && p.tma_store) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
@@ -1007,20 +974,16 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             uint32_t stage = 0, phase = 0;
             bool ok = true;
             for (uint32_t t = pair; ok && t < T; t += npairs) {
-                uint32_t width = kPairBN;
-                const PairTile tg = kTail ? pair_tile_tail(p, t, &width) : pair_tile<kGrouped>(p, t, gpre);
+                const PairTile tg = pair_tile<kGrouped>(p, t, gpre);
                 const int32_t a_row = (int32_t)(tg.a_row + rank * 128);
-                const int32_t b_row = (int32_t)(tg.b_row + rank * (width / 2));
-                const bool narrow = kTail && width != kPairBN;
-                // both CTAs' bytes: a 128-row A half and a width/2-row B half each
-                const uint32_t stage_tx = 2 * (kPairHalfBytes + (width / 2) * kPairBK);
+                const int32_t b_row = (int32_t)(tg.b_row + rank * 128);
                 for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
                     if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = full_bar + 8 * stage;
-                    if (rank == 0) mbar_arrive_expect_tx(fb, stage_tx);
+                    if (rank == 0) mbar_arrive_expect_tx(fb, 2 * kPairSB);  // both CTAs' bytes
                     const uint32_t fb_leader = mapa_shared(fb, 0);
                     const uint32_t sa = sbase + stage * kPairSB;
                     const int32_t kc = (int32_t)(kb * kPairBK);
@@ -1028,8 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     // 128-byte swizzle atom along M or N: each CTA holds 128 of them)
                     if (p.a_mn_major) tma_load_2d_pair(sa, &tmA, fb_leader, a_row, kc);
                     else tma_load_2d_pair(sa, &tmA, fb_leader, kc, a_row);
-                    if (narrow) tma_load_2d_pair(sa + kPairHalfBytes, &tmBn, fb_leader, kc, b_row);
-                    else if (p.b_mn_major) tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, b_row, kc);
+                    if (p.b_mn_major) tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, b_row, kc);
                     else tma_load_2d_pair(sa + kPairHalfBytes, &tmB, fb_leader, kc, b_row);
                     if (++stage == ST) stage = 0, phase ^= 1;
                 }
@@ -1039,8 +1001,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc_full = idesc_i8(256, kPairBN, p.a_mn_major, p.b_mn_major);
-            const uint32_t idesc_narrow = kTail ? idesc_i8(256, kPairBN / p.tail_split, p.a_mn_major, 0) : 0u;
+            const uint32_t idesc = idesc_i8(256, kPairBN, p.a_mn_major, p.b_mn_major);
             // K-major: 32-byte steps inside the swizzled rows; MN-major: 32 k rows of 128 bytes
             const uint32_t a_step = p.a_mn_major ? 32 * 128 : 32, b_step = p.b_mn_major ? 32 * 128 : 32;
             const uint32_t a_lbo = p.a_mn_major ? 128 * kPairBK : 16, b_lbo = p.b_mn_major ? 128 * kPairBK : 16;
@@ -1048,7 +1009,6 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             bool ok = true;
             for (uint32_t t = pair; ok && t < T; t += npairs, ++uidx) {
                 const uint32_t buf = uidx & 1, use = uidx >> 1;
-                const uint32_t idesc = (kTail && t >= p.tail_first) ? idesc_narrow : idesc_full;
                 if (!mbar_wait(tempty_bar + 8 * buf, (use & 1) ^ 1, SITE_MMA_TMEM_EMPTY, abort_flag, wait_limit_ns)) {
                     ok = false;
                     break;
@@ -1088,9 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             const uint32_t buf = uidx & 1, use = uidx >> 1;
             if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) break;
             tc_fence_after();
-            uint32_t width = kPairBN;
-            const PairTile tg = kTail ? pair_tile_tail(p, t, &width) : pair_tile<kGrouped>(p, t, gpre);
-            const uint32_t nch = width / CW;  // 32-column chunks of this tile
+            const PairTile tg = pair_tile<kGrouped>(p, t, gpre);
             // rows past the tile's limit (the matrix, or the group) get an
             // out-of-range index so the stores skip them
             const uint32_t row0 = tg.a_row + rank * 128 + row_local;
@@ -1105,12 +1063,11 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             }
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ch += 2) {
-                if (kTail && ch >= nch) break;
                 int32_t acc0[CW], acc1[CW];
                 tmem_ld_chunk<CW>(taddr + ch * CW, acc0);
                 tmem_ld_chunk<CW>(taddr + (ch + 1) * CW, acc1);
                 tmem_ld_wait();
-                if (ch + 2 >= (kTail ? nch : NCH)) {
+                if (ch + 2 >= NCH) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
@@ -1233,9 +1190,8 @@ bool make_output_map(CUtensorMap* map, void* c, uint32_t Mk, uint32_t Nk, uint32
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kGrouped, bool G = false, bool kTail = false>
-cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, cudaStream_t st,
-                        const CUtensorMap* tbn = nullptr)
+template <bool kGrouped, bool G = false>
+cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, cudaStream_t st)
 {
     CUtensorMap tc;
     std::memset(&tc, 0, sizeof(tc));
@@ -1248,13 +1204,12 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped, G, kTail>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  pair_smem(G));
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_pair_kernel<kGrouped, G, kTail>
-        <<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, tc, tbn ? *tbn : tb, kp, kWaitLimitNs);
+    gemm_i8_pair_kernel<kGrouped, G><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, tc, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -1284,18 +1239,6 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
         s.k_blocks = (K + kPairBK - 1) / kPairBK;
         s.dp_tiles = (uint32_t)T2;
         s.ctas = (uint32_t)(2 * (T2 < pairs ? T2 : pairs));
-        // Narrow tail: a last round that fills at most half (a quarter) of the
-        // pairs runs its tiles as 2 (4) column slices instead, so that round
-        // takes about half (a quarter) of a tile time.  K-major B only (the
-        // slices' B boxes are 64 / 32 rows of 128 bytes).
-        const uint64_t rem = T2 % pairs;
-        if (!b_mn_major && rem != 0 && T2 > pairs) {
-            const uint32_t split = rem * 4 <= pairs ? 4u : rem * 2 <= pairs ? 2u : 1u;
-            if (split > 1) {
-                s.tail_first = (uint32_t)(T2 - rem);
-                s.tail_split = split;
-            }
-        }
         return;
     }
 #endif
@@ -1386,16 +1329,6 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     // The all-gather epilogue (extra destinations / multicast) is a separate
     // build of each kernel, so plain GEMMs carry none of its code.
     const bool gather = p.n_extra > 0 || p.mc_c != nullptr;
-    if (s.cta_pair && s.tail_split > 1 && !gather) {
-        CUtensorMap tbn;
-        if (!make_operand_map(&tbn, p.b, p.Nk, p.K, p.ldb, false, 128 / s.tail_split)) {
-            if (detail) *detail = "cuTensorMapEncodeTiled rejected an operand (alignment / stride)";
-            return cudaErrorInvalidValue;
-        }
-        kp.tail_first = s.tail_first;
-        kp.tail_split = s.tail_split;
-        return launch_pair<false, false, true>(ta, tb, kp, st, &tbn);
-    }
     if (s.cta_pair) return gather ? launch_pair<false, true>(ta, tb, kp, st) : launch_pair<false>(ta, tb, kp, st);
     if (gather) {
         switch (bn) {

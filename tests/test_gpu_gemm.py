@@ -91,15 +91,13 @@ def test_ragged_padded(cuda_device, M, N, K):
     run_case(M, N, K, "col", "row", pad=32, out="f16")
 
 
-# CTA-pair shapes whose last round is at most half (a quarter) full: that round
-# runs as 2 (4) column slices per tile (the narrow-tail build): 4096^2 (256 tiles,
-# 34 in the last round -> halves), 1280 x 4096 (80 -> 6 -> quarters), 16384 x 3584
-# (896 -> 8 -> quarters, config 4's 8-GPU shard), ragged 2500 x 7900 (310 -> 14,
-# slices past N), and an MN-major A.
+# CTA-pair shapes whose last round is partly filled: 4096^2 (256 tiles, 34 in
+# the last round), 1280 x 4096 (80 -> 6), 16384 x 3584 (896 -> 8, config 4's
+# 8-GPU shard), ragged 2500 x 7900 (310 -> 14, last tile past N), MN-major A.
 @pytest.mark.parametrize("M,N,K,la", [(4096, 4096, 512, "row"), (1280, 4096, 1024, "row"),
                                       (16384, 3584, 256, "row"), (2500, 7900, 512, "row"),
                                       (4096, 4096, 256, "col")])
-def test_pair_narrow_tail(cuda_device, M, N, K, la):
+def test_pair_partial_last_round(cuda_device, M, N, K, la):
     run_case(M, N, K, la, "col")
 
 
