@@ -235,7 +235,7 @@ b2sq_status b2sq_gemm_i8_plan(uint32_t m, uint32_t n, uint32_t k, b2sq_layout la
     b2sq::plan_gemm_schedule(mp.Mk, mp.Nk, k, mp.a_mn, mp.b_mn, use_stream_k != 0, num_sms, s);
     std::memset(plan, 0, sizeof(*plan));
     plan->swap_ab = mp.swap;
-    plan->tile_m = s.cta_pair ? 2 * b2sq::kTileM : s.tile_rows;
+    plan->tile_m = s.cta_pair ? 2 * b2sq::kTileM : b2sq::kTileM;
     plan->cta_pair = s.cta_pair;
     plan->tile_n = s.tile_n;
     plan->tile_k = s.tile_k;

@@ -101,11 +101,6 @@ struct KParams {
     // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
     // row scales) are written by the kernel launched just before this one.
     uint32_t pdl_dep;
-    // Rows of A per plain (non-grouped) tile: 128, or fewer for skinny
-    // HBM-bound schedules whose tiles are shortened so that every CTA streams
-    // the same number of weight rows (K-major A only; the MMA still computes
-    // 128 rows and the rows past tile_rows are not stored).
-    uint32_t tile_rows;
 };
 
 constexpr uint32_t kTileK_Grouped = tile_k_for(256);
@@ -205,9 +200,9 @@ __device__ __forceinline__ TileGeom tile_geom(const KParams& p, uint32_t t, cons
     } else {
         uint32_t tm, tn;
         tile_coords(p, t, tm, tn);
-        g.a_row = tm * p.tile_rows;
+        g.a_row = tm * kTileM;
         g.c_row = g.a_row;
-        g.row_end = g.a_row + p.tile_rows < p.Mk ? g.a_row + p.tile_rows : p.Mk;
+        g.row_end = p.Mk;
         g.b_row = tn * BN;
         g.col0 = tn * BN;
         g.cs_off = 0;
@@ -638,8 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = full_bar + 8 * stage;
-                    // a shortened tile's A box holds tile_rows rows per K atom
-                    mbar_arrive_expect_tx(fb, kGrouped ? L::SB : L::SB - (kTileM - p.tile_rows) * BK);
+                    mbar_arrive_expect_tx(fb, L::SB);
                     const uint32_t sa = sbase + stage * L::SB;
                     const uint32_t sb = sa + L::A_BYTES;
                     if (!pdl_pending) {
@@ -1280,26 +1274,8 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
         s.sk_iters = T * (uint64_t)s.k_blocks;
         s.ctas = (uint32_t)(s.sk_iters < P ? s.sk_iters : P);
     }
-    s.tile_rows = kTileM;
-    // Skinny HBM-bound tiles (decode) in more than one round: shorten the
-    // tiles so that every CTA gets the same number of them and so streams the
-    // same number of weight rows (e.g. 28672 rows: 224 tiles of 128 on 148
-    // SMs leave 76 SMs with two tiles and 72 with one; 296 tiles of 97 rows
-    // give every SM two).  K-major A only (its TMA box is rows x 128 bytes).
-    if (hbm_bound && s.sk_iters == 0 && s.tiles_n == 1 && !a_mn_major && T > P) {
-        const uint64_t units = (uint64_t)P * ((T + P - 1) / P);
-        const uint32_t rows = (uint32_t)((Mk + units - 1) / units);
-        if (rows < kTileM) {
-            s.tile_rows = rows;
-            s.tiles_m = (Mk + rows - 1) / rows;
-            s.dp_tiles = s.tiles_m;
-            s.ctas = s.tiles_m < P ? s.tiles_m : P;
-        }
-    }
     const uint64_t tail = T - s.dp_tiles;
-    if (s.tile_rows != kTileM) {
-        // (no stream-K tail on this path)
-    } else if (tail > kWsCounters) {  // more tail tiles than counters: whole tiles only
+    if (tail > kWsCounters) {  // more tail tiles than counters: whole tiles only
         s.dp_tiles = (uint32_t)T;
         s.sk_iters = 0;
         s.ctas = (uint32_t)(T < P ? T : P);
@@ -1313,7 +1289,7 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
 {
     const uint32_t bn = s.tile_n;
     CUtensorMap ta, tb;
-    if (!make_operand_map(&ta, p.a, p.Mk, p.K, p.lda, p.a_mn_major != 0, s.tile_rows ? s.tile_rows : kTileM) ||
+    if (!make_operand_map(&ta, p.a, p.Mk, p.K, p.lda, p.a_mn_major != 0, kTileM) ||
         !make_operand_map(&tb, p.b, p.Nk, p.K, p.ldb, p.b_mn_major != 0, s.cta_pair ? 128 : bn)) {
         if (detail) *detail = "cuTensorMapEncodeTiled rejected an operand (alignment / stride)";
         return cudaErrorInvalidValue;
@@ -1348,7 +1324,6 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
         kp.ws_slots = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + kWsCounterBytes);
     }
     kp.raster_group = B2SQ_RASTER_GROUP;
-    kp.tile_rows = s.tile_rows ? s.tile_rows : kTileM;
     kp.pdl_dep = s.cta_pair ? 0u : (uint32_t)p.pdl_dep;  // the pair kernel is launched without PDL
     if (kp.ctas == 0) return cudaSuccess;
     // The all-gather epilogue (extra destinations / multicast) is a separate
@@ -1410,7 +1385,6 @@ cudaError_t launch_gemm_i8_grouped(const GroupedProblem& g, uint32_t num_sms, cu
     kp.row_scale = g.row_scale;
     kp.col_scale = g.col_scale;
     kp.raster_group = 1;
-    kp.tile_rows = kTileM;
     kp.grp_start = g.group_start;
     kp.grp_count = g.group_count;
     kp.groups = g.groups;

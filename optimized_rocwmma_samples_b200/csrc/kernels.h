@@ -58,7 +58,6 @@ struct GemmSchedule {
     uint32_t dp_tiles;
     uint64_t sk_iters;
     size_t workspace_bytes;  // bytes of workspace the schedule needs (0 without stream-K)
-    uint32_t tile_rows;      // A rows per 1-CTA tile (128, fewer for balanced decode tiles)
 };
 
 // Stream-K is used only when whole-tile rounds would leave more than this

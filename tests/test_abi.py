@@ -120,9 +120,7 @@ def test_schedule_covers_each_kblock_once(m, n, k, sk):
 def test_plan_choices():
     p = api.plan(16, 28672, 8192, num_sms=148)
     # decode: skinny tiles are HBM-bound, whole tiles only (no stream-K)
-    # weight tiles shortened to 97 rows so that each of the 148 CTAs streams two (296 x 97 >= 28672)
-    assert p.swap_ab == 1 and p.tile_n == 16 and p.tile_m == 97 and p.tiles_m == 296 and p.dp_tiles == 296
-    assert p.sk_iters == 0 and p.ctas == 148
+    assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 224 and p.sk_iters == 0
     p = api.plan(100, 4096, 4096, num_sms=148)
     assert p.swap_ab == 1 and p.tile_n == 128 and p.dp_tiles == 0  # compute-bound small problem: all stream-K
     p = api.plan(8192, 8192, 8192, num_sms=148)
