@@ -101,13 +101,6 @@ struct KParams {
     // Programmatic dependent launch: 0 none, 1 / 2 = the A / B operand (and the
     // row scales) are written by the kernel launched just before this one.
     uint32_t pdl_dep;
-    // CTA-pair stream-K tail (gemm_i8_pair_kernel<.., kSK = true>): the
-    // pair tiles from pair_sk_first on (the last, partly filled round) are
-    // each split along K into pair_sk_split slices, one pair per slice; each
-    // slice's partial tile goes to a workspace slot and the pair whose slice
-    // completes the tile sums the slots and stores it.
-    uint32_t pair_sk_first;
-    uint32_t pair_sk_split;
 };
 
 constexpr uint32_t kTileK_Grouped = tile_k_for(256);
@@ -856,7 +849,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // most 5% of the pairs idle.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kPairBN = 256;  // tile columns (MMA N)
-constexpr uint64_t kPairMaxSlices = 4;  // K-slices per tile of the stream-K tail
 constexpr uint32_t kPairBK = 128;
 constexpr uint32_t kPairHalfBytes = 128 * kPairBK;          // 16 KiB: one operand half per stage
 constexpr uint32_t kPairSB = 2 * kPairHalfBytes;            // A half + B half per CTA per stage
@@ -911,28 +903,11 @@ __device__ __forceinline__ PairTile pair_tile(const KParams& p, uint32_t t, cons
     return g;
 }
 
-// Work unit t of the pair schedule: a whole tile, or (stream-K tail build)
-// K-slice `slice` of tile `tile`, k-blocks [k0, k1).
-struct PairUnit {
-    uint32_t tile, k0, k1, slice;
-    bool partial;
-};
-
-template <bool kSK>
-__device__ __forceinline__ PairUnit pair_unit(const KParams& p, uint32_t t)
-{
-    if (!kSK || t < p.pair_sk_first) return PairUnit{t, 0u, p.k_blocks, 0u, false};
-    const uint32_t j = t - p.pair_sk_first, S = p.pair_sk_split;
-    const uint32_t sl = j % S;
-    return PairUnit{p.pair_sk_first + j / S, sl * p.k_blocks / S, (sl + 1) * p.k_blocks / S, sl, true};
-}
-
-template <bool kGrouped, bool G = false, bool kSK = false>
+template <bool kGrouped, bool G = false>
 __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const KParams p, uint64_t wait_limit_ns)
 {
-    static_assert(!kSK || (!kGrouped && !G), "the stream-K tail is a plain-GEMM build");
     constexpr uint32_t ST = kPairST;
     constexpr uint32_t TMEM_COLS = 512;  // two 256-column accumulators
     extern __shared__ uint8_t smem_raw[];
@@ -951,8 +926,6 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
     const uint32_t pair = blockIdx.x >> 1;
     const uint32_t npairs = gridDim.x >> 1;
     uint32_t T = p.tiles_m * p.tiles_n;
-    if constexpr (kSK) T = p.pair_sk_first + (T - p.pair_sk_first) * p.pair_sk_split;
-    volatile int* epi_flag = reinterpret_cast<volatile int*>(smem + kPairBarOff + 16 * kPairST + 40);
     const uint32_t* gpre = nullptr;  // grouped mode: pair-tile prefix per group, [groups + 1]
     if constexpr (kGrouped) {
         __shared__ uint32_t s_gpre[kMaxGroups + 1];
@@ -1001,11 +974,10 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             uint32_t stage = 0, phase = 0;
             bool ok = true;
             for (uint32_t t = pair; ok && t < T; t += npairs) {
-                const PairUnit pu = pair_unit<kSK>(p, t);
-                const PairTile tg = pair_tile<kGrouped>(p, pu.tile, gpre);
+                const PairTile tg = pair_tile<kGrouped>(p, t, gpre);
                 const int32_t a_row = (int32_t)(tg.a_row + rank * 128);
                 const int32_t b_row = (int32_t)(tg.b_row + rank * 128);
-                for (uint32_t kb = pu.k0; kb < pu.k1; ++kb) {
+                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
                     if (!mbar_wait(empty_bar + 8 * stage, phase ^ 1, SITE_PRODUCER_EMPTY, abort_flag, wait_limit_ns)) {
                         ok = false;
                         break;
@@ -1043,8 +1015,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + buf * kPairBN;
-                const PairUnit pu = pair_unit<kSK>(p, t);
-                for (uint32_t kb = pu.k0; kb < pu.k1; ++kb) {
+                for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
                     if (!mbar_wait(full_bar + 8 * stage, phase, SITE_MMA_FULL, abort_flag, wait_limit_ns)) {
                         ok = false;
                         break;
@@ -1055,7 +1026,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
                     for (uint32_t kk = 0; kk < kPairBK / 32; ++kk) {
                         const uint64_t ad = umma_desc_sw128(sa + kk * a_step, a_lbo, 1024);
                         const uint64_t bd = umma_desc_sw128(sa + kPairHalfBytes + kk * b_step, b_lbo, 1024);
-                        mma_i8_pair(d_tmem, ad, bd, idesc, (kb > pu.k0 || kk > 0) ? 1u : 0u);
+                        mma_i8_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                     }
                     mma_commit_pair(empty_bar + 8 * stage, 0x3);
                     if (++stage == ST) stage = 0, phase ^= 1;
@@ -1077,8 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             const uint32_t buf = uidx & 1, use = uidx >> 1;
             if (!mbar_wait(tfull_bar + 8 * buf, use & 1, SITE_EPI_TMEM_FULL, abort_flag, wait_limit_ns)) break;
             tc_fence_after();
-            const PairUnit pu = pair_unit<kSK>(p, t);
-            const PairTile tg = pair_tile<kGrouped>(p, pu.tile, gpre);
+            const PairTile tg = pair_tile<kGrouped>(p, t, gpre);
             // rows past the tile's limit (the matrix, or the group) get an
             // out-of-range index so the stores skip them
             const uint32_t row0 = tg.a_row + rank * 128 + row_local;
@@ -1090,63 +1060,6 @@ __global__ void __launch_bounds__(kThreads, 1) __cluster_dims__(2, 1, 1)
             for (uint32_t ch = 0; ch < NCH; ++ch) {
                 const uint32_t col = tg.col0 + ch * CW + lane;
                 csv[ch] = p.col_scale_vec ? (col < p.Nk ? __ldg(p.col_scale_vec + tg.cs_off + col) : 0.f) : p.col_scale;
-            }
-            if constexpr (kSK) {
-                if (pu.partial) {
-                    // This CTA's 128 x 256 half of a K-slice: to its workspace
-                    // slot, column-major so a warp's stores are 128-byte runs.
-                    const uint32_t slices = p.pair_sk_split;
-                    const uint32_t tail = pu.tile - p.pair_sk_first;
-                    constexpr size_t kHalf = 128 * kPairBN;
-                    int32_t* my = p.ws_slots + ((size_t)(tail * slices + pu.slice) * 2 + rank) * kHalf;
-#pragma unroll 1
-                    for (uint32_t ch = 0; ch < NCH; ++ch) {
-                        int32_t acc[CW];
-                        tmem_ld_chunk<CW>(taddr + ch * CW, acc);
-                        tmem_ld_wait();
-                        if (ch + 1 == NCH) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar + 8 * buf, 0));
-                        }
-#pragma unroll
-                        for (uint32_t jj = 0; jj < CW; ++jj) __stcg(my + (size_t)(ch * CW + jj) * 128 + row_local, acc[jj]);
-                    }
-                    __threadfence();
-                    named_bar_sync(1, kEpiThreads);
-                    if (threadIdx.x == 64) {
-                        uint32_t* cnt = p.ws_cnt + tail * 2 + rank;
-                        const uint32_t old = atomicAdd(cnt, 1u);
-                        const int last = (old + 1 == slices) ? 1 : 0;
-                        if (last) *cnt = 0;  // every slice has arrived: ready for the next call
-                        *epi_flag = last;
-                    }
-                    named_bar_sync(1, kEpiThreads);
-                    if (!*epi_flag) continue;
-                    // This slice completed the tile half: sum every slice's slot
-                    // (int32, exact, order free) and store it like a whole tile.
-                    __threadfence();
-                    const int32_t* base = p.ws_slots + ((size_t)(tail * slices) * 2 + rank) * kHalf;
-#pragma unroll 1
-                    for (uint32_t ch = 0; ch < NCH; ch += 2) {
-                        int32_t acc0[CW], acc1[CW];
-#pragma unroll
-                        for (uint32_t jj = 0; jj < CW; ++jj) acc0[jj] = acc1[jj] = 0;
-#pragma unroll 1
-                        for (uint32_t sl = 0; sl < slices; ++sl) {
-                            const int32_t* src = base + (size_t)sl * 2 * kHalf;
-#pragma unroll
-                            for (uint32_t jj = 0; jj < CW; ++jj) {
-                                acc0[jj] += __ldcg(src + (size_t)(ch * CW + jj) * 128 + row_local);
-                                acc1[jj] += __ldcg(src + (size_t)((ch + 1) * CW + jj) * 128 + row_local);
-                            }
-                        }
-                        const uint32_t brow0 = tg.a_row + rank * 128 + q * 32;
-                        store_pair<CW, G>(p, row, tg.col0 + ch * CW, acc0, acc1, rsc, csv[ch], csv[ch + 1], epi_stage,
-                                          tmc, brow0, brow0 + 32 <= tg.row_end || tg.row_end >= p.Mk);
-                    }
-                    continue;
-                }
             }
 #pragma unroll
             for (uint32_t ch = 0; ch < NCH; ch += 2) {
@@ -1277,7 +1190,7 @@ bool make_output_map(CUtensorMap* map, void* c, uint32_t Mk, uint32_t Nk, uint32
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kGrouped, bool G = false, bool kSK = false>
+template <bool kGrouped, bool G = false>
 cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, cudaStream_t st)
 {
     CUtensorMap tc;
@@ -1291,12 +1204,12 @@ cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, KParams kp
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done_mask.load() & bit)) {
-        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped, G, kSK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemm_i8_pair_kernel<kGrouped, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  pair_smem(G));
         if (e != cudaSuccess) return e;
         done_mask.fetch_or(bit);
     }
-    gemm_i8_pair_kernel<kGrouped, G, kSK><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, tc, kp, kWaitLimitNs);
+    gemm_i8_pair_kernel<kGrouped, G><<<kp.ctas, kThreads, pair_smem(G), st>>>(ta, tb, tc, kp, kWaitLimitNs);
     return cudaGetLastError();
 }
 
@@ -1326,20 +1239,6 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
         s.k_blocks = (K + kPairBK - 1) / kPairBK;
         s.dp_tiles = (uint32_t)T2;
         s.ctas = (uint32_t)(2 * (T2 < pairs ? T2 : pairs));
-        // Stream-K tail: a last round that fills at most half of the pairs
-        // runs its tiles as S K-slices each (S pairs per tile), so the round
-        // takes about 1/S of a tile time plus the slot traffic of the fix-up.
-        const uint64_t rem = T2 % pairs;
-        if (allow_stream_k && rem != 0 && T2 > pairs && rem * 2 <= pairs && rem <= kWsCounters / 2) {
-            uint64_t S = pairs / rem;
-            if (S > kPairMaxSlices) S = kPairMaxSlices;
-            if (S > s.k_blocks) S = s.k_blocks;
-            if (S >= 2) {
-                s.pair_sk_first = (uint32_t)(T2 - rem);
-                s.pair_sk_split = (uint32_t)S;
-                s.workspace_bytes = kWsCounterBytes + (size_t)rem * S * 2 * 128 * kPairBN * sizeof(int32_t);
-            }
-        }
         return;
     }
 #endif
@@ -1430,11 +1329,6 @@ cudaError_t launch_gemm_i8(const GemmProblem& p, const GemmSchedule& s, void* wo
     // The all-gather epilogue (extra destinations / multicast) is a separate
     // build of each kernel, so plain GEMMs carry none of its code.
     const bool gather = p.n_extra > 0 || p.mc_c != nullptr;
-    if (s.cta_pair && s.pair_sk_split > 1 && !gather) {
-        kp.pair_sk_first = s.pair_sk_first;
-        kp.pair_sk_split = s.pair_sk_split;
-        return launch_pair<false, false, true>(ta, tb, kp, st);
-    }
     if (s.cta_pair) return gather ? launch_pair<false, true>(ta, tb, kp, st) : launch_pair<false>(ta, tb, kp, st);
     if (gather) {
         switch (bn) {

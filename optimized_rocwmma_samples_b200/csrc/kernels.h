@@ -58,8 +58,6 @@ struct GemmSchedule {
     uint32_t dp_tiles;
     uint64_t sk_iters;
     size_t workspace_bytes;  // bytes of workspace the schedule needs (0 without stream-K)
-    uint32_t pair_sk_first;  // CTA pairs: first tile of the K-sliced last round
-    uint32_t pair_sk_split;  // CTA pairs: K-slices per tile in that round (0/1: none)
 };
 
 // Stream-K is used only when whole-tile rounds would leave more than this
