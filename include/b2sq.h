@@ -189,12 +189,17 @@ B2SQ_API b2sq_status b2sq_smoothquant_gemm_i8(const void* x_f16, const float* sm
  * column-major), scales as in b2sq_gemm_i8 (vectors may be null), h_c
  * row-major.  The problem is cut into row_chunks x col_chunks output blocks
  * (0 = chosen from the shape); the host->device copies, the block GEMMs and
- * the device->host copies of finished blocks overlap on the caller's stream
- * and two copy streams the library keeps per device.  dev_buffer (256-byte
- * aligned, b2sq_gemm_i8_host_buffer_size bytes) holds the device copies;
+ * the device->host copies of finished blocks overlap on three streams the
+ * library keeps per device; the caller's stream waits for the last copy
+ * back.  dev_buffer (256-byte aligned, b2sq_gemm_i8_host_buffer_size bytes) holds the device copies;
  * nothing is allocated.  Host memory should be pinned for the copies to
  * overlap.  Enqueues only: h_c is complete once `stream` has been
- * synchronised.  k % 16 == 0.  One call at a time per device.
+ * synchronised.  k % 16 == 0.  The copies into dev_buffer are ordered after
+ * this function's previous call on the same buffer, not after other work
+ * queued on `stream`: alternate two buffers to overlap consecutive calls
+ * (the next inputs go up while the previous result comes down), and do not
+ * use dev_buffer for anything else.  Calls are enqueued one at a time per
+ * device (host lock).
  */
 B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k,
                                        const int8_t* h_a, const int8_t* h_w,

@@ -227,7 +227,9 @@ gemm_quant_tensor_scale = gemm_quant
 
 # ----------------------------------------------------------------------------- MoE
 class HostGemmBuffers:
-    """The device buffer gemm_quant_host reuses (one per shape, dtype and device)."""
+    """The two device buffers gemm_quant_host alternates between (one pair per
+    shape, dtype and device): consecutive calls use different buffers, so the
+    next call's inputs go up while the previous call's result comes down."""
 
     def __init__(self, m: int, n: int, k: int, out_dtype: torch.dtype, device: torch.device):
         self.key = (m, n, k, out_dtype, device)
@@ -235,7 +237,13 @@ class HostGemmBuffers:
         size = C.c_size_t(0)
         _lib.check(lib.b2sq_gemm_i8_host_buffer_size(m, n, k, _DTYPE_CODE[out_dtype], C.byref(size)),
                    "b2sq_gemm_i8_host_buffer_size")
-        self.buf = torch.empty((size.value,), dtype=torch.uint8, device=device)
+        self.bufs = [torch.empty((size.value,), dtype=torch.uint8, device=device) for _ in range(2)]
+        self.turn = 0
+
+    def next(self) -> torch.Tensor:
+        buf = self.bufs[self.turn]
+        self.turn ^= 1
+        return buf
 
 
 def gemm_quant_host(h_a: torch.Tensor, h_w_nk: torch.Tensor, h_sa: torch.Tensor, h_sb: torch.Tensor,
@@ -263,8 +271,9 @@ def gemm_quant_host(h_a: torch.Tensor, h_w_nk: torch.Tensor, h_sa: torch.Tensor,
     key = (M, N, K, out_dtype, dev)
     b = buffers if buffers is not None and buffers.key == key else HostGemmBuffers(M, N, K, out_dtype, dev)
     lib = _lib.load()
+    buf = b.next()
     st = lib.b2sq_gemm_i8_host(M, N, K, h_a.data_ptr(), h_w_nk.data_ptr(), h_sa.data_ptr(), h_sb.data_ptr(), 1.0,
-                               1.0, h_c.data_ptr(), _DTYPE_CODE[out_dtype], b.buf.data_ptr(), b.buf.numel(),
+                               1.0, h_c.data_ptr(), _DTYPE_CODE[out_dtype], buf.data_ptr(), buf.numel(),
                                int(chunks), int(chunks if col_chunks is None else col_chunks),
                                _stream_ptr(None, dev))
     _lib.check(st, "b2sq_gemm_i8_host")

@@ -8,14 +8,17 @@
 // against each other and against the GEMMs on three streams:
 //
 //   copy-in stream   A_0, B_0, A_1, B_1, ...   (+ scales)
-//   caller's stream  on each arrival, one GEMM over the strip of blocks it
+//   GEMM stream      on each arrival, one GEMM over the strip of blocks it
 //                    completes (A_i: blocks (i, j) of the B chunks already
 //                    in; B_j: blocks (i, j) of the A chunks already in)
 //   copy-out stream  each strip back to the host (pitched copy) once computed
 //
 // so the first block leaves the device after 1/row_chunks of A and
 // 1/col_chunks of B have arrived, and host->device and device->host traffic
-// overlap for most of the call (PCIe is full duplex).  Nothing is allocated:
+// overlap for most of the call (PCIe is full duplex).  The caller's stream
+// waits for the last copy back.  Consecutive calls on two alternating device
+// buffers overlap as well: a call's copies in and GEMMs wait only for the
+// previous call on the same buffer.  Nothing is allocated:
 // the caller passes one device buffer of b2sq_gemm_i8_host_buffer_size bytes.
 // The copy streams and events are created once per device and reused.
 #include "../../include/b2sq.h"
@@ -62,14 +65,20 @@ std::vector<uint32_t> cuts(uint32_t len, uint32_t chunks)
     return c;
 }
 
-// Measured at 8192^3 (bf16 out, B200, PCIe 5): 2x2 4.19 ms, 4x4 3.73, 8x8 3.81, 16x16 4.09, 32x32 4.73;
-// finer blocks start the copy back sooner but make the pitched copies and the
-// block GEMMs less efficient.
-uint32_t auto_chunks(uint32_t len) { return len >= 2048 ? 4 : len >= 1024 ? 2 : 1; }
+// Measured at 8192^3 (bf16 out, B200, PCIe 5), one call / ten back-to-back
+// calls on alternating buffers, ms per call: 1x1 5.18 / 3.17, 2x2 4.13 / 3.20,
+// 3x3 3.77 / 3.19, 4x4 3.70 / 3.31, 8x8 3.72 / 3.29.  Finer blocks start the
+// copy back sooner within one call; between calls the overlap of one call's
+// copy back with the next call's copies in does that already, and finer
+// pitched copies cost bandwidth.
+uint32_t auto_chunks(uint32_t len) { return len >= 2048 ? 3 : len >= 1024 ? 2 : 1; }
 
 struct DeviceCtx {
     bool ready = false;
-    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaStream_t s_in = nullptr, s_out = nullptr, s_mm = nullptr;
+    // Per device buffer: the event after the last copy-back of the previous
+    // call that used it (its GEMMs precede that copy-back).
+    std::vector<std::pair<void*, cudaEvent_t>> buf_done;
     std::vector<cudaEvent_t> ev;  // grown on demand
     std::mutex mu;                 // one call at a time per device
 };
@@ -137,13 +146,14 @@ B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k, const
         std::lock_guard<std::mutex> lock(g_ctx_mu);
         if ((e = cudaStreamCreateWithFlags(&d.s_in, cudaStreamNonBlocking)) != cudaSuccess) return cuda_err(e, "stream");
         if ((e = cudaStreamCreateWithFlags(&d.s_out, cudaStreamNonBlocking)) != cudaSuccess) return cuda_err(e, "stream");
+        if ((e = cudaStreamCreateWithFlags(&d.s_mm, cudaStreamNonBlocking)) != cudaSuccess) return cuda_err(e, "stream");
         d.ready = true;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const std::vector<uint32_t> rc = cuts(m, row_chunks ? row_chunks : auto_chunks(m));
     const std::vector<uint32_t> cc = cuts(n, col_chunks ? col_chunks : auto_chunks(n));
     const size_t mi = rc.size() - 1, nj = cc.size() - 1;
-    // events: [0] start, [1, 1+mi) A_i in, [1+mi, 1+mi+nj) B_j in, then one per strip, then copy-out done
+    // events: [0] unused, [1, 1+mi) A_i in, [1+mi, 1+mi+nj) B_j in, then one per strip, then copy-out done
     const size_t ev_a = 1, ev_w = ev_a + mi, ev_c = ev_w + nj, ev_done = ev_c + mi + nj;
     if ((e = events(d, ev_done + 1)) != cudaSuccess) return cuda_err(e, "events");
     uint8_t* base = static_cast<uint8_t*>(dev_buffer);
@@ -161,9 +171,21 @@ B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k, const
     } while (0)
 
     // the copies start after whatever the caller enqueued before (earlier use of the buffer)
-    B2SQ_TRY(cudaEventRecord(d.ev[0], st), "record");
-    B2SQ_TRY(cudaStreamWaitEvent(d.s_in, d.ev[0], 0), "wait");
-    B2SQ_TRY(cudaStreamWaitEvent(d.s_out, d.ev[0], 0), "wait");
+    // The copies into dev_buffer wait only for this library's previous call on
+    // the same buffer (its GEMMs and copy-back), not for everything queued on
+    // `stream`: calls on two alternating buffers overlap, the next call's
+    // inputs going up while the previous call's result comes down.
+    cudaEvent_t done = nullptr;
+    for (auto& bd : d.buf_done)
+        if (bd.first == dev_buffer) done = bd.second;
+    const bool first_use = done == nullptr;
+    if (first_use) {
+        B2SQ_TRY(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "events");
+        d.buf_done.emplace_back(dev_buffer, done);
+    } else {
+        B2SQ_TRY(cudaStreamWaitEvent(d.s_in, done, 0), "wait");
+        B2SQ_TRY(cudaStreamWaitEvent(d.s_mm, done, 0), "wait");
+    }
     if (d_sb) B2SQ_TRY(cudaMemcpyAsync(d_sb, h_scale_b_col, (size_t)n * 4, cudaMemcpyHostToDevice, d.s_in), "copy in");
     // Input chunks arrive alternately (A_0, B_0, A_1, B_1, ...): every block
     // needs one chunk of each, so after f of the input bytes about f^2 of the
@@ -197,7 +219,7 @@ B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k, const
     // (its A rows or B rows are contiguous) and one pitched copy back.
     size_t na = 0, nb = 0, strip = 0;
     for (const Arrival& ar : order) {
-        B2SQ_TRY(cudaStreamWaitEvent(st, d.ev[ar.is_a ? ev_a + ar.idx : ev_w + ar.idx], 0), "wait");
+        B2SQ_TRY(cudaStreamWaitEvent(d.s_mm, d.ev[ar.is_a ? ev_a + ar.idx : ev_w + ar.idx], 0), "wait");
         uint32_t r0, r1, c0, c1;
         if (ar.is_a) {
             r0 = rc[ar.idx], r1 = rc[ar.idx + 1], c0 = 0, c1 = cc[nb];
@@ -211,9 +233,9 @@ B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k, const
         b2sq_status s = b2sq_gemm_i8(r1 - r0, c1 - c0, k, d_a + (size_t)r0 * k, B2SQ_ROW_MAJOR, k,
                                      d_w + (size_t)c0 * k, B2SQ_COL_MAJOR, k, cblk, c_type, n,
                                      d_sa ? d_sa + r0 : nullptr, d_sb ? d_sb + c0 : nullptr, scale_a, scale_b,
-                                     nullptr, 0, stream);
+                                     nullptr, 0, reinterpret_cast<b2sq_stream_t>(d.s_mm));
         if (s != B2SQ_OK) return s;
-        B2SQ_TRY(cudaEventRecord(d.ev[ev_c + strip], st), "record");
+        B2SQ_TRY(cudaEventRecord(d.ev[ev_c + strip], d.s_mm), "record");
         B2SQ_TRY(cudaStreamWaitEvent(d.s_out, d.ev[ev_c + strip], 0), "wait");
         B2SQ_TRY(cudaMemcpy2DAsync(static_cast<uint8_t*>(h_c) + ((size_t)r0 * n + c0) * esz, (size_t)n * esz, cblk,
                                    (size_t)n * esz, (size_t)(c1 - c0) * esz, r1 - r0, cudaMemcpyDeviceToHost,
@@ -223,6 +245,7 @@ B2SQ_API b2sq_status b2sq_gemm_i8_host(uint32_t m, uint32_t n, uint32_t k, const
     }
     // the caller's stream completes when the result is in host memory
     B2SQ_TRY(cudaEventRecord(d.ev[ev_done], d.s_out), "record");
+    B2SQ_TRY(cudaEventRecord(done, d.s_out), "record");
     B2SQ_TRY(cudaStreamWaitEvent(st, d.ev[ev_done], 0), "wait");
 #undef B2SQ_TRY
     return B2SQ_OK;
