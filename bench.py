@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the 2 s sustained loop (for profiler runs)")
     ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64"], default=None,
                     help="run 3 launches of one kernel on its workload and exit (for ncu captures)")
     return ap.parse_args()
@@ -374,7 +375,7 @@ def main():
     # ---------------- sustained: the same GEMM back to back for >= 2 s (no flush), clocks sampled.
     # Last, so that the power-capped, hot state it leaves behind does not colour the other numbers.
     sus = None
-    if world == 1:
+    if world == 1 and not args.no_sustained:
         n_sus = max(50, int(2.0 / (ms_max * 1e-3)) + 1)
         torch.cuda.synchronize()
         with ClockSampler(local_rank, interval=0.01) as clk_sus:
