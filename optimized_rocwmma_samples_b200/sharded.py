@@ -109,7 +109,11 @@ def multicast_supported(device: torch.device) -> bool:
 
 
 def cuda_ops(out_dtype: torch.dtype = torch.bfloat16, gather: str = "auto") -> Ops:
-    """gather: how the fused GEMM + all-gather reaches the other ranks --
+    """The quantised activations, row scales and GEMM output live in buffers
+    kept per shape and reused by the next call of the same shape (as a layer's
+    workspace would be): a returned tensor is valid until that next call.
+
+    gather: how the fused GEMM + all-gather reaches the other ranks --
     "multicast" (NVSwitch multimem stores, one copy per output piece),
     "ipc" (plain stores into every peer's buffer), or "auto" (= "ipc", the
     faster of the two at 2 and at 8 GPUs)."""
@@ -157,10 +161,28 @@ def cuda_ops(out_dtype: torch.dtype = torch.bfloat16, gather: str = "auto") -> O
             if isinstance(po, PeerOutput):
                 po.close()
         peers.clear()
+        bufs.clear()
+
+    bufs: dict = {}  # per-shape activation and output buffers, reused by later calls
+
+    def buf(key, shape, dtype, dev):
+        k = (key, tuple(shape), dtype, dev)
+        if k not in bufs:
+            bufs[k] = torch.empty(shape, dtype=dtype, device=dev)
+        return bufs[k]
+
+    def smoothquant(x, s):
+        m, k = x.shape
+        return api.smoothquant(x, s, y=buf("xq", (m, k), torch.int8, x.device),
+                               row_scale=buf("rs", (m,), torch.float32, x.device))
+
+    def gemm(xq, w, sa, sb):
+        c = buf("out", (xq.shape[0], w.shape[0]), out_dtype, xq.device)
+        return api.gemm_quant(xq, w.t(), sa, sb, out_dtype=out_dtype, c=c, workspace=ws)
 
     return Ops(
-        smoothquant=lambda x, s: api.smoothquant(x, s),
-        gemm=lambda xq, w, sa, sb: api.gemm_quant(xq, w.t(), sa, sb, out_dtype=out_dtype, workspace=ws),
+        smoothquant=smoothquant,
+        gemm=gemm,
         gemm_gather=gemm_gather,
         close=close,
     )
