@@ -143,6 +143,10 @@ class ClockSampler:
 
     def __enter__(self):
         if self._h is not None:
+            # the sampling thread must get the interpreter often enough to take
+            # several samples in a region of a few milliseconds
+            self._switch = sys.getswitchinterval()
+            sys.setswitchinterval(1e-4)
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
@@ -151,6 +155,7 @@ class ClockSampler:
         if self._h is not None:
             self._stop.set()
             self._t.join()
+            sys.setswitchinterval(self._switch)
 
     def summary(self):
         if not self.samples:
