@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-sustained", action="store_true", help="skip the 2 s sustained loop (for profiler runs)")
-    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64"], default=None,
+    ap.add_argument("--profile", choices=["gemm", "smoothquant", "decode16", "decode64", "grouped"], default=None,
                     help="run 3 launches of one kernel on its workload and exit (for ncu captures)")
     return ap.parse_args()
 
@@ -80,6 +80,16 @@ def run_profile(kind: str):
         s = torch.ones((SQ_K,), device=dev)
         for _ in range(3):
             api.smoothquant(x, s)
+    elif kind == "grouped":  # config 5's grouped GEMM: 8 experts x 1024 routed rows, 14336 x 4096 each
+        E, H, NI, seg = 8, 4096, 14336, 1024
+        w5 = synth.torch_int8_uniform((E, NI, H), dev, 55)
+        sb5 = synth.torch_scales(E * NI, dev, 56)
+        qy = synth.torch_int8_uniform((E * seg, H), dev, 7)
+        rs = synth.torch_scales(E * seg, dev, 8)
+        start = torch.arange(0, E * seg + 1, seg, dtype=torch.int32, device=dev)
+        cnt = torch.full((E,), seg, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            api.gemm_grouped(qy, w5, start, cnt, rs, sb5, out_dtype=torch.bfloat16)
     else:
         m = {"gemm": M, "decode16": 16, "decode64": 64}[kind]
         n = N if kind == "gemm" else 28672
