@@ -138,17 +138,20 @@ class ClockSampler:
         except Exception:  # NVML unavailable: clocks reported as null
             self._h = None
 
-    def _run(self):
+    def _sample(self):
         nv = self._nv
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                for name, bit in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
+            self._sample()
             time.sleep(self.interval)
 
     def __enter__(self):
@@ -166,6 +169,7 @@ class ClockSampler:
             self._stop.set()
             self._t.join()
             sys.setswitchinterval(self._switch)
+            self._sample()  # the clock as the region ends (it changes over milliseconds, not microseconds)
 
     def summary(self):
         if not self.samples:
