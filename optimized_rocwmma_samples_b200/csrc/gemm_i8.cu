@@ -1221,13 +1221,16 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
     s = GemmSchedule{};
     const uint32_t P = num_sms ? num_sms : 148;
 #ifndef B2SQ_DISABLE_PAIR
-    // CTA-pair 256 x 256 tiles for every problem of at least 256 x 256 (either
+    // CTA-pair 256 x 256 tiles for every problem of more than 128 x 128 (either
     // operand K-major or MN-major): a 1-CTA 128 x 256 tile streams 1.5x the operand bytes per MMA and
     // is L2-bound (ncu: 57-60% against 84% tensor utilisation), so pairs win
-    // even when most of their last round is idle (measured on B200, in us,
-    // pairs vs 1-CTA stream-K: 4096^3 57.9 vs 82.4; 512 x 8192 x 8192 37.3 vs
-    // 76.3; 1280 x 4096 x 8192, 46% of the last round idle, 53.8 vs 57.8).
-    if (Mk >= 256 && Nk >= 256 && P >= 2) {
+    // even when most of their last round is idle, or most of their tile rows
+    // or columns lie past the matrix (measured on B200, in us, pairs vs 1-CTA
+    // tiles: 4096^3 57.9 vs 82.4; 512 x 8192 x 8192 37.3 vs 76.3; 1280 x 4096
+    // x 8192 53.8 vs 57.8; 200 x 8192 x 4096 31.6 vs 51.2; 160 x 28672 x 8192
+    // 61.3 vs 108.6; 129 x 8192 x 8192 41.0 vs 57.3; 8192 x 200 x 8192 47.1 vs
+    // 55.3; 16384 x 192 x 2048 32.8 vs 45.1).
+    if (Mk > kTileM && Nk > kTileM && P >= 2) {
         const uint64_t tm2 = (Mk + 255) / 256, tn2 = (Nk + kPairBN - 1) / kPairBN, T2 = tm2 * tn2;
         const uint64_t pairs = P / 2;
         s.cta_pair = 1;
@@ -1259,7 +1262,16 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
     // splitting tiles gains nothing and its fix-up costs a few microseconds
     // (measured).  Stream-K is for compute-bound tails.
     const bool hbm_bound = bn <= 64;
-    if (!allow_stream_k || hbm_bound || s.k_blocks < 2 || tail_loss <= kStreamKMinTailLoss) {
+    // A split tile is summed by the CTA whose slice completes it, which reads
+    // every contributor's slot in turn, so stream-K pays only while a tile has
+    // at most ~3 contributors (measured, us, stream-K vs whole tiles: 128 x 8192
+    // x 8192 (64 tiles) 41.0 vs 45.0; 100 x 4096 x 4096 (32 tiles) 38.9 vs 34.8;
+    // 120 x 640 x 4096 (5 tiles) 100.5 vs 34.8; 100 x 200 x 8192 (1 tile) 354.5
+    // vs 57.4; 96 x 28672 x 8192 (224 tiles, 1.5 rounds) 68.5 vs 59.4).
+    const uint64_t tail_tiles = T % P;
+    const bool few_contributors = tail_tiles * kStreamKMaxContributors >= P;
+    if (!allow_stream_k || hbm_bound || s.k_blocks < 2 || tail_loss <= kStreamKMinTailLoss || !few_contributors ||
+        (T > P && T < 4ull * P)) {
         s.dp_tiles = (uint32_t)T;
         s.sk_iters = 0;
         s.ctas = (uint32_t)(T < P ? T : P);
@@ -1269,7 +1281,7 @@ void plan_gemm_schedule(uint32_t Mk, uint32_t Nk, uint32_t K, uint32_t a_mn_majo
         s.sk_iters = (T - s.dp_tiles) * (uint64_t)s.k_blocks;
         s.ctas = P;
     } else {
-        // Few rounds: stream-K over everything keeps every SM busy to the end.
+        // Less than one round: stream-K over everything keeps every SM busy to the end.
         s.dp_tiles = 0;
         s.sk_iters = T * (uint64_t)s.k_blocks;
         s.ctas = (uint32_t)(s.sk_iters < P ? s.sk_iters : P);

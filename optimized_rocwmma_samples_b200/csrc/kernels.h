@@ -63,6 +63,8 @@ struct GemmSchedule {
 // Stream-K is used only when whole-tile rounds would leave more than this
 // fraction of the last round's SM time idle.
 constexpr double kStreamKMinTailLoss = 0.05;
+// ... and only while each split tile has at most about this many contributing CTAs.
+constexpr uint64_t kStreamKMaxContributors = 3;
 
 // Stream-K workspace layout: a fixed header of per-tile k-block counters at
 // offset 0 (zero before the first call; every call leaves them zero), then

@@ -100,7 +100,7 @@ def simulate_units(pl):
 
 
 @pytest.mark.parametrize("m,n,k", [(8192, 8192, 8192), (16, 28672, 8192), (64, 28672, 8192),
-                                   (16384, 28672, 8192), (19 * 128, 20 * 256, 1024), (1, 16, 16), (512, 8192, 8192), (200, 8192, 1024),
+                                   (16384, 28672, 8192), (19 * 128, 20 * 256, 1024), (1, 16, 16), (512, 8192, 8192), (200, 8192, 1024), (128, 8192, 8192),
                                    (3000, 3000, 3000), (128, 128, 128 * 1000)])
 @pytest.mark.parametrize("sk", [True, False])
 def test_schedule_covers_each_kblock_once(m, n, k, sk):
@@ -121,8 +121,12 @@ def test_plan_choices():
     p = api.plan(16, 28672, 8192, num_sms=148)
     # decode: skinny tiles are HBM-bound, whole tiles only (no stream-K)
     assert p.swap_ab == 1 and p.tile_n == 16 and p.tiles_m == 224 and p.dp_tiles == 224 and p.sk_iters == 0
+    p = api.plan(128, 8192, 8192, num_sms=148)
+    assert p.swap_ab == 1 and p.tile_n == 128 and p.dp_tiles == 0  # 64 tiles, under a round: all stream-K
     p = api.plan(100, 4096, 4096, num_sms=148)
-    assert p.swap_ab == 1 and p.tile_n == 128 and p.dp_tiles == 0  # compute-bound small problem: all stream-K
+    assert p.swap_ab == 1 and p.dp_tiles == 32 and p.sk_iters == 0  # 32 tiles: > 3 contributors each, whole tiles
+    p = api.plan(96, 28672, 8192, num_sms=148)
+    assert p.dp_tiles == 224 and p.sk_iters == 0  # 1.5 rounds: whole tiles
     p = api.plan(8192, 8192, 8192, num_sms=148)
     # CTA pairs: 1024 tiles of 256 x 256 over 74 pairs, 14 rounds, 1.2% idle
     assert p.cta_pair == 1 and p.swap_ab == 0 and p.tile_m == 256 and p.tile_n == 256
@@ -134,7 +138,10 @@ def test_plan_choices():
     p = api.plan(512, 8192, 8192, num_sms=148)
     assert p.cta_pair == 1 and p.dp_tiles == 64 and p.ctas == 128  # fewer tiles than pairs: one tile per pair
     p = api.plan(200, 8192, 1024, num_sms=148)
-    # fewer rows than a pair tile, not skinny enough to swap: 1-CTA 128 x 256 tiles, all stream-K
+    # more than 128 rows, not skinny enough to swap: CTA pairs (rows past 200 are zero-filled)
+    assert p.cta_pair == 1 and p.tiles_m == 1 and p.tiles_n == 32 and p.sk_iters == 0
+    p = api.plan(100, 16384, 2048, api.COL_MAJOR, api.COL_MAJOR, num_sms=148)
+    # column-major A is not swapped: 1-CTA 128 x 256 tiles, 64 of them, all stream-K
     assert p.cta_pair == 0 and p.tile_n == 256 and p.dp_tiles == 0 and p.sk_iters == 64 * p.k_blocks
     p = api.plan(8192, 8192, 8192, api.ROW_MAJOR, api.ROW_MAJOR, num_sms=148)
     assert p.tile_n in (128, 256)

@@ -103,15 +103,18 @@ def test_pair_partial_last_round(cuda_device, M, N, K, la):
 
 @pytest.mark.parametrize("stream_k", [True, False])
 def test_stream_k_equivalence(cuda_device, stream_k):
-    # 200 rows: fewer than a CTA-pair tile, too many to swap -> 1-CTA 128 x 256 tiles,
-    # 2 x 32 = 64 tiles over 148 SMs: all stream-K (or whole tiles without a workspace)
-    run_case(200, 8192, 1024, stream_k=stream_k)
+    # 128 x 8192, swapped: 64 1-CTA tiles of 128 x 128 over 148 SMs, all stream-K
+    # (or whole tiles without a workspace); and 100 x 16384 with column-major A
+    # (not swapped): 64 tiles of 128 x 256, all stream-K
+    assert api.plan(128, 8192, 1024).sk_iters > 0 or not stream_k
+    run_case(128, 8192, 1024, stream_k=stream_k)
+    run_case(100, 16384, 1024, la="col", stream_k=stream_k)
 
 
 def test_stream_k_workspace_reuse(cuda_device):
     # repeated calls reuse the same workspace; it must come back zeroed
     for i in range(3):
-        run_case(16, 28672, 1024, out="f16", seed=i)
+        run_case(128, 8192, 2048, out="f16", seed=i)
 
 
 def test_tensor_scale_mode(cuda_device):

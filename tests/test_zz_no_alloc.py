@@ -28,25 +28,27 @@ def ulp_dist(a_bits, b_bits):
 
 
 def no_alloc(a, w, sa, sb, out_dtype):
-    """C = a @ w.t() through the C ABI entry point that allocates nothing."""
+    """C = a @ w.t() through the C ABI entry point that allocates nothing
+    (a row-major, or a column-major view such as t.t() of a [K, lda] buffer)."""
     lib = _lib.load()
     M, K = a.shape
     N = w.shape[0]
     c = torch.empty((M, N), dtype=out_dtype, device=a.device)
     code = {torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.int32: _lib.I32}[out_dtype]
-    st = lib.b2sq_gemm_i8_no_alloc(M, N, K, a.data_ptr(), _lib.ROW_MAJOR, K, w.data_ptr(), _lib.COL_MAJOR, K,
+    la, lda = (_lib.ROW_MAJOR, a.stride(0)) if a.stride(1) == 1 else (_lib.COL_MAJOR, a.stride(1))
+    st = lib.b2sq_gemm_i8_no_alloc(M, N, K, a.data_ptr(), la, lda, w.data_ptr(), _lib.COL_MAJOR, K,
                                    c.data_ptr(), code, N, sa.data_ptr(), sb.data_ptr(), 1.0, 1.0,
                                    torch.cuda.current_stream().cuda_stream)
     return st, c
 
 
-# (100, 4096, 4096): swapped 128-wide tiles, all stream-K (~19 MiB of scratch);
+# (128, 8192, 8192): swapped 128-wide tiles, all stream-K (~19 MiB of scratch);
 # (16, 28672, 8192): decode, no scratch needed; (8192, 8192, 1024): whole tiles.
-@pytest.mark.parametrize("M,N,K", [(100, 4096, 4096), (16, 28672, 8192), (8192, 8192, 1024)])
+@pytest.mark.parametrize("M,N,K", [(128, 8192, 8192), (16, 28672, 8192), (8192, 8192, 1024)])
 def test_no_alloc_matches_workspace_entry_point(cuda_device, M, N, K):
     dev = cuda_device
     # the first shape must really use the static scratch, the decode shape none
-    if (M, N, K) == (100, 4096, 4096):
+    if (M, N, K) == (128, 8192, 8192):
         assert api.workspace_size(M, N, K) > 0
     if (M, N, K) == (16, 28672, 8192):
         assert api.workspace_size(M, N, K) == 0
@@ -70,13 +72,14 @@ def test_no_alloc_matches_workspace_entry_point(cuda_device, M, N, K):
 
 
 def test_no_alloc_rejects_oversized_scratch(cuda_device):
-    # 200 x 8192 x 2048: fewer rows than a CTA-pair tile, too many to swap the operands:
-    # 1-CTA 128 x 256 tiles, 64 of them over 148 SMs, all stream-K: ~39 MiB of scratch (> 24 MiB)
+    # 100 x 16384 x 2048 with column-major A (not swapped): 1-CTA 128 x 256 tiles, 64 of
+    # them over 148 SMs, all stream-K: ~39 MiB of scratch (> 24 MiB)
     dev = cuda_device
-    a = synth.torch_int8_uniform((200, 2048), dev, 1)
-    w = synth.torch_int8_uniform((8192, 2048), dev, 2)
-    sa, sb = synth.torch_scales(200, dev, 3), synth.torch_scales(8192, dev, 4)
-    need = api.workspace_size(200, 8192, 2048)
+    at = synth.torch_int8_uniform((2048, 112), dev, 1)  # A^T with a 16-aligned leading dimension
+    a = at[:, :100].t()
+    w = synth.torch_int8_uniform((16384, 2048), dev, 2)
+    sa, sb = synth.torch_scales(100, dev, 3), synth.torch_scales(16384, dev, 4)
+    need = api.workspace_size(100, 16384, 2048, api.COL_MAJOR, api.COL_MAJOR)
     assert need > 24 << 20
     st, _ = no_alloc(a, w, sa, sb, torch.float16)
     assert st == _lib.B2SQ_ERR_UNSUPPORTED
