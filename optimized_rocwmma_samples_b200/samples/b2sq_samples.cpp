@@ -209,6 +209,60 @@ static void test_quant_gemm(uint32_t m, uint32_t n, uint32_t k)
     if (ws) CHECK_CUDA(cudaFree(ws));
 }
 
+// The reference driver's copy-in / kernel / copy-back sequence (rocwmma_gemm_quantized.cpp:214-218)
+// through the host-buffer entry: operands and result in pinned host memory,
+// ten calls back to back on two alternating device buffers, mean time per call
+// with every copy in the timed region.  K-major weights, per-row x per-column
+// scales (all 1/127), bf16 out.
+static void test_quant_gemm_host(uint32_t m, uint32_t n, uint32_t k)
+{
+    int8_t *hA, *hW;
+    float *hSa, *hSb;
+    uint16_t* hC;
+    CHECK_CUDA(cudaMallocHost(&hA, (size_t)m * k));
+    CHECK_CUDA(cudaMallocHost(&hW, (size_t)n * k));
+    CHECK_CUDA(cudaMallocHost(&hSa, (size_t)m * 4));
+    CHECK_CUDA(cudaMallocHost(&hSb, (size_t)n * 4));
+    CHECK_CUDA(cudaMallocHost(&hC, (size_t)m * n * 2));
+    std::memset(hA, 1, (size_t)m * k);
+    std::memset(hW, 1, (size_t)n * k);
+    for (uint32_t i = 0; i < m; ++i) hSa[i] = 1.f / 127.f;
+    for (uint32_t j = 0; j < n; ++j) hSb[j] = 1.f / 127.f;
+    size_t buf_bytes = 0;
+    CHECK_B2SQ(b2sq_gemm_i8_host_buffer_size(m, n, k, B2SQ_BF16, &buf_bytes));
+    void* dbuf[2];
+    CHECK_CUDA(cudaMalloc(&dbuf[0], buf_bytes));
+    CHECK_CUDA(cudaMalloc(&dbuf[1], buf_bytes));
+    int call = 0;
+    auto fn = [&] {
+        CHECK_B2SQ(b2sq_gemm_i8_host(m, n, k, hA, hW, hSa, hSb, 1.f, 1.f, hC, B2SQ_BF16, dbuf[call & 1], buf_bytes, 0,
+                                     0, nullptr));
+        ++call;
+    };
+    const double ms = bench(fn, 3, 10);
+    const double tflops = 2.0 * m * n * k / (ms * 1e-3) / 1e12;
+    std::printf("[QuantGEMM-I8-host] M=%u N=%u K=%u  %g ms  %g TFlops/s\n", m, n, k, ms, tflops);
+    // Known answer: every output is bf16(k * (1/127 * 1/127)).
+    CHECK_CUDA(cudaDeviceSynchronize());
+    const float want = (float)k * ((1.f / 127.f) * (1.f / 127.f));
+    uint32_t bits;
+    std::memcpy(&bits, &want, 4);
+    const uint16_t want16 = (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);  // round to nearest even
+    bool ok = true;
+    for (size_t i = 0; i < (size_t)m * n; ++i) ok = ok && hC[i] == want16;
+    if (!ok) {
+        std::printf("[QuantGEMM-I8-host] known answer FAILED\n");
+        ++g_failures;
+    }
+    CHECK_CUDA(cudaFree(dbuf[0]));
+    CHECK_CUDA(cudaFree(dbuf[1]));
+    CHECK_CUDA(cudaFreeHost(hA));
+    CHECK_CUDA(cudaFreeHost(hW));
+    CHECK_CUDA(cudaFreeHost(hSa));
+    CHECK_CUDA(cudaFreeHost(hSb));
+    CHECK_CUDA(cudaFreeHost(hC));
+}
+
 static void test_moe_sorting(uint32_t tokens, uint32_t experts, uint32_t topk, uint32_t unit)
 {
     std::mt19937 rng(42);
@@ -330,6 +384,7 @@ int main(int argc, char** argv)
         test_quant_gemm(3840, 4096, 4096);
         test_quant_gemm(4096, 4096, 4096);
         test_quant_gemm(8192, 8192, 8192);
+        test_quant_gemm_host(8192, 8192, 8192);
     }
     if (what == "sorting" || what == "all") {
         std::printf("=== MoE Sorting (b2sq, sm_100a) ===\n");

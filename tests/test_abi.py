@@ -185,3 +185,29 @@ def test_allgather_and_ipc_validation_without_gpu():
     assert lib.b2sq_ipc_export(None, h, C.byref(off)) == _lib.B2SQ_ERR_INVALID_ARG
     assert lib.b2sq_ipc_open(None, None) == _lib.B2SQ_ERR_INVALID_ARG
     assert lib.b2sq_ipc_close(None) == _lib.B2SQ_ERR_INVALID_ARG
+
+
+def test_host_gemm_entry_validation_without_gpu():
+    """b2sq_gemm_i8_host checks its arguments before any CUDA call."""
+    lib = _lib.load()
+    size = C.c_size_t(0)
+    assert lib.b2sq_gemm_i8_host_buffer_size(8192, 8192, 8192, _lib.BF16, C.byref(size)) == _lib.B2SQ_OK
+    # A, B, both scale vectors and C, each rounded up to 256 bytes
+    assert size.value >= 8192 * 8192 * 2 + 8192 * 8192 * 2 + 2 * 8192 * 4
+    h = (C.c_int8 * 4096)()
+    hf = (C.c_float * 64)()
+    c = (C.c_uint16 * 4096)()
+    big = (C.c_uint8 * 4096)()
+    # null output
+    assert lib.b2sq_gemm_i8_host(64, 64, 64, h, h, hf, hf, 1.0, 1.0, None, _lib.BF16, big, 4096, 0, 0,
+                                 None) == _lib.B2SQ_ERR_INVALID_ARG
+    # k not a multiple of 16 (TMA)
+    assert lib.b2sq_gemm_i8_host(8, 8, 24, h, h, hf, hf, 1.0, 1.0, c, _lib.BF16, big, 4096, 0, 0,
+                                 None) == _lib.B2SQ_ERR_UNSUPPORTED
+    # device buffer smaller than b2sq_gemm_i8_host_buffer_size
+    assert lib.b2sq_gemm_i8_host(64, 64, 64, h, h, hf, hf, 1.0, 1.0, c, _lib.BF16, big, 16, 0, 0,
+                                 None) == _lib.B2SQ_ERR_INVALID_ARG
+    assert b"buffer" in lib.b2sq_last_error_message()
+    # empty problem: nothing to do
+    assert lib.b2sq_gemm_i8_host(0, 64, 64, None, None, None, None, 1.0, 1.0, None, _lib.BF16, None, 0, 0, 0,
+                                 None) == _lib.B2SQ_OK

@@ -25,6 +25,7 @@ def test_samples_driver(cuda_device):
     assert len(tags.get("SmoothQuant", [])) == 4
     assert len(tags.get("MoE-SmoothQuant", [])) == 3
     assert len(tags.get("QuantGEMM-I8", [])) == 3
+    assert len(tags.get("QuantGEMM-I8-host", [])) == 1
     assert len(tags.get("MoE Sorting", [])) == 5
     assert len(tags.get("TopK-Softmax", [])) == 5
     assert "FAILED" not in res.stdout
