@@ -302,6 +302,25 @@ def main():
         torch.cuda.synchronize()
         return max_over_ranks(statistics.mean(a_.elapsed_time(b_) for a_, b_ in evs))
 
+    def timed_interleaved(fns, n):
+        """Mean device ms of each fn over n rounds that run every fn once in turn
+        (L2 flushed before each), max over ranks."""
+        for f in fns:
+            f()
+        ms_ = [[] for _ in fns]
+        barrier()
+        torch.cuda.synchronize()
+        for _ in range(n):
+            for i, f in enumerate(fns):
+                l2_flush()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                f()
+                e1.record(stream)
+                ms_[i].append((e0, e1))
+        torch.cuda.synchronize()
+        return [max_over_ranks(statistics.mean(a_.elapsed_time(b_) for a_, b_ in evs)) for evs in ms_]
+
     # inputs: same activations on every rank, a distinct weight shard per rank
     a = synth.torch_int8_uniform((M, K), dev, 11)
     w = synth.torch_int8_uniform((N, K), dev, 100 + rank)  # [N_shard, K] K-major
@@ -353,7 +372,7 @@ def main():
         extra = n1_sections(args, dev, api, synth, timed, l2_flush, stream, hbm_gbs, ws)
 
     # ---------------- config 4: N-sharded prefill (strong scaling over the ranks)
-    c4 = c4_section(dev, world, rank, api, synth, timed)
+    c4 = c4_section(dev, world, rank, api, synth, timed, timed_interleaved)
 
     # ---------------- e2e through the C ABI from pinned host buffers
     h_a = a.cpu().pin_memory()
@@ -521,7 +540,7 @@ def n1_sections(args, dev, api, synth, timed, l2_flush, stream, hbm_gbs, ws):
 PEER_GBS = 770.0
 
 
-def c4_section(dev, world, rank, api, synth, timed):
+def c4_section(dev, world, rank, api, synth, timed, timed_interleaved):
     """Config 4: 16384 x 8192 x 28672, smoothquant + int8 GEMM, N-sharded.
 
     t1_*: the whole N on one GPU (every rank runs it alone, max over ranks);
@@ -545,21 +564,25 @@ def c4_section(dev, world, rank, api, synth, timed):
     w_full = synth.torch_int8_uniform((PN, K), dev, 40)
     sb_full = synth.torch_scales(PN, dev, 50)
     c_full = torch.empty((PM, PN), dtype=torch.bfloat16, device=dev)
-    t1_gemm = timed(lambda: api.gemm_quant(xq, w_full.t(), rs, sb_full, out_dtype=torch.bfloat16, c=c_full), 5)
     xq1, rs1 = torch.empty_like(xq), torch.empty_like(rs)
+
+    def gemm1():
+        api.gemm_quant(xq, w_full.t(), rs, sb_full, out_dtype=torch.bfloat16, c=c_full)
 
     def step1():
         api.smoothquant(x, s, y=xq1, row_scale=rs1)
         api.gemm_quant(xq1, w_full.t(), rs1, sb_full, out_dtype=torch.bfloat16, c=c_full)
 
-    t1_step = timed(step1, 5)
     n0, n1 = shard_range(PN, world, rank)
     w_sh = w_full[n0:n1].contiguous()
     sb_sh = sb_full[n0:n1].contiguous()
-    del w_full, c_full, xq1, rs1
     layer = ShardedPrefill(w_sh, sb_sh, PN, cuda_ops(torch.bfloat16))
-    tN_gemm = timed(lambda: layer.ops.gemm(xq, layer.w, rs, layer.sb), 10)
-    tN_step = timed(lambda: layer.forward(x, s, PM, K, "replicated", False), 10)
+    # the whole-N and the sharded runs alternate step by step, so both see the
+    # same power and clock state (a 2.4 ms GEMM heats the part measurably)
+    t1_gemm, tN_gemm, t1_step, tN_step = timed_interleaved(
+        [gemm1, lambda: layer.ops.gemm(xq, layer.w, rs, layer.sb),
+         step1, lambda: layer.forward(x, s, PM, K, "replicated", False)], 6)
+    del w_full, c_full, xq1, rs1
     out.update({"t1_gemm_ms": r4(t1_gemm), "tN_gemm_ms": r4(tN_gemm), "speedup_sharded_gemm": r4(t1_gemm / tN_gemm),
                 "t1_step_ms": r4(t1_step), "tN_step_ms": r4(tN_step), "speedup_step": r4(t1_step / tN_step),
                 "tN_gemm_tops": r4(ops_pf / (tN_gemm * 1e-3) / 1e12)})
