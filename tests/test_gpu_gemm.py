@@ -220,3 +220,31 @@ def test_gemm_from_host_buffers(cuda_device, M, N, K, chunks):
         bufs = api.gemm_quant_host(*h, h_c, out_dtype=torch.bfloat16, chunks=chunks, buffers=bufs)
         torch.cuda.synchronize()
         assert torch.equal(h_c, ref.cpu())
+
+
+def test_host_entry_int32_without_scales(cuda_device):
+    """b2sq_gemm_i8_host through the C ABI with int32 output and no scale
+    vectors (ragged shape, 2 x 3 blocks): equals b2sq_gemm_i8 on device tensors."""
+    import ctypes as C
+
+    from optimized_rocwmma_samples_b200 import _lib, api, synth
+
+    dev = cuda_device
+    M, N, K = 300, 520, 272
+    a = synth.torch_int8_uniform((M, K), dev, 21)
+    w = synth.torch_int8_uniform((N, K), dev, 22)
+    ref = api.gemm_quant(a, w.t(), out_dtype=torch.int32)
+    h_a, h_w = a.cpu().pin_memory(), w.cpu().pin_memory()
+    h_c = torch.zeros((M, N), dtype=torch.int32).pin_memory()
+    lib = _lib.load()
+    size = C.c_size_t(0)
+    assert lib.b2sq_gemm_i8_host_buffer_size(M, N, K, _lib.I32, C.byref(size)) == _lib.B2SQ_OK
+    buf = torch.empty((size.value,), dtype=torch.uint8, device=dev)
+    for _ in range(2):
+        h_c.zero_()
+        st = lib.b2sq_gemm_i8_host(M, N, K, h_a.data_ptr(), h_w.data_ptr(), None, None, 1.0, 1.0, h_c.data_ptr(),
+                                   _lib.I32, buf.data_ptr(), buf.numel(), 2, 3,
+                                   torch.cuda.current_stream().cuda_stream)
+        assert st == _lib.B2SQ_OK, lib.b2sq_last_error_message()
+        torch.cuda.synchronize()
+        assert torch.equal(h_c, ref.cpu())
